@@ -1,0 +1,145 @@
+/*
+ * torch_ans_b200.h -- C ABI of the B200 rANS coding engine (libtorch_ans_b200.so).
+ *
+ * Every entry point takes plain device pointers, element counts and a CUDA stream handle
+ * (cudaStream_t passed as void*; NULL = the legacy default stream).  No torch types cross this
+ * boundary.  All coding calls are asynchronous on the given stream; nothing here synchronises the
+ * device unless its comment says so.  All tensors are int32, row-major and densely packed.
+ *
+ * Stream rows use the reference's layout (torch_ans/rans_cpu.cpp:81-84,181): an int32 matrix of
+ * shape (batch, stream_width); row[0] holds the payload length in bytes, row[1..] the payload:
+ * the coder state(s) little-endian, then the emitted words appended upward.
+ *
+ * Return value of every int function: TANS_OK (0) or one of the TANS_E_* codes.  Problems that
+ * can only be seen on the device (an index outside the table list, a symbol outside its table
+ * without escape coding, a zero frequency, a row that is too short) never cause an out-of-bounds
+ * access: the kernel skips that step and ORs a TANS_DEV_* bit into *dev_status (when non-NULL).
+ */
+#ifndef TORCH_ANS_B200_H
+#define TORCH_ANS_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Coder variants: (state bits, word bits).  The three template instantiations bound at
+ * torch_ans/rans.hpp:297-322 (rans64 = <uint64_t,uint32_t>, rans32 = <uint32_t,uint8_t>,
+ * rans32_16 = <uint32_t,uint16_t>). */
+#define TANS_RANS64 0
+#define TANS_RANS32 1
+#define TANS_RANS32_16 2
+
+/* Symbol lookup used by pop (torch_ans/rans_utils.hpp:412-450): bisection on the cdf row,
+ * inverse-cdf table at row + cdf_size, or alias table at row + cdf_size. */
+#define TANS_LOOKUP_SEARCH 0
+#define TANS_LOOKUP_INVCDF 1
+#define TANS_LOOKUP_ALIAS 2
+
+/* Host-visible return codes. */
+#define TANS_OK 0
+#define TANS_E_INVALID_ARGUMENT 1
+#define TANS_E_CUDA 2
+#define TANS_E_WORKSPACE 3
+#define TANS_E_TOO_LARGE 4
+
+/* Device-side error bits (ORed into *dev_status). */
+#define TANS_DEV_BAD_INDEX 1u
+#define TANS_DEV_BAD_VALUE 2u
+#define TANS_DEV_OVERFLOW 4u
+#define TANS_DEV_UNDERFLOW 8u
+#define TANS_DEV_BAD_FREQ 16u
+#define TANS_DEV_BAD_ESCAPE 32u
+
+/* Library version, (major << 16) | (minor << 8) | patch. */
+int tans_version(void);
+
+/* Human-readable name of a return code. */
+const char* tans_status_string(int code);
+
+/* Bytes of device scratch that tans_push needs for a table list of num_tables rows of cdf_width
+ * entries (a per-entry reciprocal table plus per-table size/offset pairs). */
+size_t tans_push_workspace_size(int variant, int64_t num_tables, int64_t cdf_width);
+
+/* Encode: push num_symbols symbols per stream row onto `stream`, last symbol first.
+ * Replaces the reference's rans_push<State, Word, USE_ALIAS, I> (torch_ans/rans.hpp:84-217) after
+ * its resize step, i.e. rans_push_indexed_cpu (torch_ans/rans_cpu.cpp:44-189) /
+ * rans_push_indexed_cuda (torch_ans/rans_cuda.cu:115-167).
+ *   stream      [batch, stream_width] int32, updated in place (length, state, appended words);
+ *               the caller sizes stream_width for the worst case, as rans.hpp:105-124 does.
+ *   symbols     [batch, num_symbols], indexes [batch, num_symbols]: table index per symbol.
+ *   cdfs        [num_tables, cdf_width]: quantised cdf rows (with use_alias: the remap rows made
+ *               by rans_alias_build_table, remap at row + cdf_size).
+ *   cdf_sizes   [num_tables], offsets [num_tables] (offsets may be NULL = all zero).
+ *   num_interleaves 1, or 4 for the 4-state format of the *_i4 ops (rans_cpu.cpp:89-160).
+ *   workspace   device scratch of tans_push_workspace_size() bytes, 256-byte aligned; NULL makes
+ *               the call allocate and free it stream-ordered (cudaMallocAsync / cudaFreeAsync).
+ *   dev_status  device uint32 receiving TANS_DEV_* bits, or NULL. */
+int tans_push(int variant, int use_alias, int num_interleaves,
+              int32_t* stream, int64_t batch, int64_t stream_width,
+              const int32_t* symbols, const int32_t* indexes, int64_t num_symbols,
+              const int32_t* cdfs, int64_t num_tables, int64_t cdf_width,
+              const int32_t* cdf_sizes, const int32_t* offsets,
+              int freq_precision, int bypass_coding, int bypass_precision,
+              void* workspace, size_t workspace_bytes, uint32_t* dev_status, void* cuda_stream);
+
+/* Bytes of device scratch that tans_pop needs (per-table size/offset pairs and, for the lookup
+ * tables it builds, their device copies). */
+size_t tans_pop_workspace_size(int variant, int lookup, int64_t num_tables, int64_t cdf_width,
+                               int freq_precision);
+
+/* Decode: pop num_symbols symbols per stream row, first symbol first, writing them to
+ * out_symbols [batch, num_symbols] and updating each row's length and state in place.
+ * Replaces rans_pop<State, Word, USE_ALIAS, USE_INVCDF, I> (torch_ans/rans.hpp:220-276), i.e.
+ * rans_pop_indexed_cpu (torch_ans/rans_cpu.cpp:191-322) / rans_pop_indexed_cuda
+ * (torch_ans/rans_cuda.cu:236-286).  With TANS_LOOKUP_ALIAS, cdfs are the table rows made by
+ * rans_alias_build_table; with TANS_LOOKUP_INVCDF each row is [cdf | inverse cdf (2^fp)]. */
+int tans_pop(int variant, int lookup, int num_interleaves,
+             int32_t* stream, int64_t batch, int64_t stream_width,
+             int32_t* out_symbols, const int32_t* indexes, int64_t num_symbols,
+             const int32_t* cdfs, int64_t num_tables, int64_t cdf_width,
+             const int32_t* cdf_sizes, const int32_t* offsets,
+             int freq_precision, int bypass_coding, int bypass_precision,
+             void* workspace, size_t workspace_bytes, uint32_t* dev_status, void* cuda_stream);
+
+/* Maximum of column 0 (payload length) over the batch rows, written to *out_max (device int32).
+ * The device half of the worst-case resize at torch_ans/rans.hpp:105-107. */
+int tans_stream_max_length(const int32_t* stream, int64_t batch, int64_t stream_width,
+                           int32_t* out_max, void* cuda_stream);
+
+/* Fill `stream` [batch, stream_width] as a fresh stream: row[0] = num_interleaves*state bytes,
+ * each state = the lower bound, zeros elsewhere.  Device version of rans_init_stream
+ * (torch_ans/rans_cpu.cpp:22-41). */
+int tans_init_stream(int variant, int num_interleaves, int32_t* stream, int64_t batch,
+                     int64_t stream_width, void* cuda_stream);
+
+/* Concatenated-bitstream assembly, the device form of rans_stream_to_byte_strings followed by
+ * merge_bytes (torch_ans/rans.cpp:5-21, torch_ans/utils.py:47-72).  Given the exclusive byte
+ * offsets of each row's record in `out` (record = optional little-endian length prefix of
+ * prefix_bytes (0, 1, 2, 4 or 8) followed by the row's payload[0:len]), writes all records.
+ * `prefix_rows` says how many leading rows get a prefix (rows >= prefix_rows get none). */
+int tans_gather_payloads(const int32_t* stream, int64_t batch, int64_t stream_width,
+                         const int64_t* record_offsets, int prefix_bytes, int64_t prefix_rows,
+                         uint8_t* out, void* cuda_stream);
+
+/* Inverse of tans_gather_payloads: rows of `stream` [batch, stream_width] are zeroed and filled
+ * with payload bytes taken from `in` at payload_offsets[b] (lengths[b] bytes each), row[0] set to
+ * lengths[b].  Device form of rans_byte_strings_to_stream (torch_ans/rans.cpp:23-53). */
+int tans_scatter_payloads(const uint8_t* in, const int64_t* payload_offsets,
+                          const int32_t* lengths, int32_t* stream, int64_t batch,
+                          int64_t stream_width, void* cuda_stream);
+
+/* Zero-frequency repair of quantised cdf rows (the per-row loop of
+ * rans_pmf_to_quantized_cdf_cpu, torch_ans/rans_cpu.cpp:351-379): for every symbol whose
+ * frequency is 0, borrow one count from the first symbol holding the smallest frequency > 1.
+ * cdfs [rows, n + 1] updated in place; rows with nothing to borrow set TANS_DEV_BAD_FREQ. */
+int tans_cdf_fix_zero_freqs(int32_t* cdfs, int64_t rows, int64_t n, uint32_t* dev_status,
+                            void* cuda_stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TORCH_ANS_B200_H */

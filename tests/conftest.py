@@ -1,0 +1,14 @@
+"""Test configuration: registers the ``gpu`` marker and puts the repository root on sys.path.
+
+Tests marked ``gpu`` need a CUDA device (a B200); everything else runs on the CPU.
+"""
+import os
+import sys
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a CUDA device (B200); run with -m gpu")
