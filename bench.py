@@ -1,0 +1,420 @@
+"""Benchmark of the rANS coding path: encode + decode Gsymbols/s on 1..8 B200 (one process per GPU).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload mixture_invcdf] [--impl ours|reference]
+
+A step is one pass of the coding path over one batch: push (encode) of every stream from a fresh
+stream tensor, then pop (decode) of every stream, through the `_C` op surface, with inputs
+resident in HBM.  ``value`` = symbols of all ranks / max-over-ranks device time of K steps
+(each symbol is encoded once and decoded once per step), in Gsymbols/s.  The default workload
+is the 2^31-symbol rans64 push + inverse-cdf pop configuration (8,192 streams x 262,144
+symbols, 256 tables over 1,024 symbols) per GPU: streams are independent, so N GPUs process N
+such batches (weak scaling) with no collective on the data path.
+
+Also reported:
+  * ``e2e``: the same round trip through the public API from pinned host memory -- H2D of symbols
+    and indexes, push, device assembly of the concatenated bitstream, D2H of it; H2D of the
+    bitstream and indexes, device parse, pop, D2H of the decoded symbols -- host wall clock, max
+    over ranks.  With N > 1 the ranks all-gather per-stream byte lengths (NCCL) to place their
+    segments in the job-wide bitstream.
+  * ``roofline``: the dominant kernel's algorithmic bytes (symbol + index + compressed bytes per
+    symbol, plus its tables) over its CUDA-event time, against the measured HBM copy bandwidth.
+  * ``cpu_baseline``: the reference CPU implementation (compiled by oracle/build_ref.py) on a
+    bounded sample of the same workload, all host threads.
+``--impl reference`` times only that reference CPU implementation (rank 0), on the same
+workload and metric.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+METRIC = "encode & decode Gsymbols/s at 1/2/4/8 B200, bit-exact vs reference CPU"
+UNIT = "Gsymbols/s"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="mixture_invcdf")
+    ap.add_argument("--scale", type=float, default=1.0, help="fraction of the configuration's streams")
+    ap.add_argument("--length-scale", type=float, default=1.0, help="fraction of the configuration's stream length")
+    ap.add_argument("--e2e-steps", type=int, default=2)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0, help="target CPU work of the baseline sample")
+    return ap.parse_args()
+
+
+def dist_setup():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if ws > 1:
+        torch.cuda.set_device(local)
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(0)
+    return ws, rank, local
+
+
+def max_over_ranks(x: float, ws: int) -> float:
+    if ws == 1:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(ws):
+    if ws > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle sampling during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        try:
+            self.gpu = "GPU-" + str(torch.cuda.get_device_properties(gpu_index).uuid)
+        except Exception:
+            self.gpu = str(gpu_index)
+        self.proc = None
+        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_rank{gpu_index}.csv")
+
+    def __enter__(self):
+        try:
+            os.makedirs(os.path.dirname(self.path), exist_ok=True)
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                          "-lms", "100"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            self.f.close()
+
+    def summary(self):
+        out = {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        try:
+            rows = [l.split(",") for l in open(self.path).read().strip().splitlines() if l.strip()]
+        except Exception:
+            return out
+        rows = [[c.strip() for c in r] for r in rows if len(r) >= 9]
+        if not rows:
+            return out
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = set()
+        for r in rows:
+            for n, v in zip(names, r[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        out.update(sm_mhz=statistics.median(sm) if sm else None, sm_max_mhz=max(mx) if mx else None,
+                   reasons=sorted(reasons), samples=len(rows))
+        return out
+
+
+def measured_peak_hbm():
+    try:
+        d = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def build_workload(name, device, scale, length_scale, seed_offset=0):
+    from torch_ans_b200 import workloads as W
+    fn = W.BUILDERS[name]
+    kw = dict(device=device, scale=scale)
+    if name != "gaussian_latent":
+        kw["length_scale"] = length_scale
+    if seed_offset:
+        import inspect
+        kw["seed"] = inspect.signature(fn).parameters["seed"].default + seed_offset
+    return fn(**kw)
+
+
+# ----------------------------------------------------------------------------- our GPU path
+def run_ours(args, ws, rank, local):
+    from torch_ans_b200 import _C
+    dev = torch.device("cuda", local)
+    w = build_workload(args.workload, dev, args.scale, args.length_scale, seed_offset=1000 * rank)
+    B, N = w.symbols.shape
+    nsym = B * N
+    push = getattr(_C, w.push_op)
+    pop = getattr(_C, w.pop_op)
+    init = getattr(_C, f"{w.variant}_init_stream")
+    kw = dict(freq_precision=w.fp, bypass_coding=w.bypass, bypass_precision=w.bp)
+    init_cpu = init(B)
+    push_t, pop_t = w.tables_for_push(), w.tables_for_pop()
+
+    def step(ev=None):
+        st = init_cpu.to(dev, non_blocking=True)
+        if ev:
+            ev[0].record()
+        push(st, w.symbols, w.indexes, push_t, w.cdfs_sizes, w.offsets, **kw)
+        if ev:
+            ev[1].record()
+        comp = st[:, 0].clone()
+        dec = pop(st, w.indexes, pop_t, w.cdfs_sizes, w.offsets, **kw)
+        if ev:
+            ev[2].record()
+        return dec, comp
+
+    for _ in range(args.warmup):
+        dec, comp = step()
+    torch.cuda.synchronize()
+    ok = bool(torch.equal(dec, w.symbols))
+    sb = 8 if w.variant == "rans64" else 4
+    comp_bytes = float((comp.to(torch.int64) - sb).sum().item())
+    del dec
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        barrier(ws)
+        t0.record()
+        for k in range(args.steps):
+            dec, comp = step(evs[k])
+        t1.record()
+        barrier(ws)
+    ok = ok and bool(torch.equal(dec, w.symbols))
+    del dec
+    ms = t0.elapsed_time(t1) / args.steps
+    push_ms = sum(e[0].elapsed_time(e[1]) for e in evs) / args.steps
+    pop_ms = sum(e[1].elapsed_time(e[2]) for e in evs) / args.steps
+    ms_max = max_over_ranks(ms, ws)
+    push_ms_max, pop_ms_max = max_over_ranks(push_ms, ws), max_over_ranks(pop_ms, ws)
+    all_ok = max_over_ranks(0.0 if ok else 1.0, ws) == 0.0
+    total = nsym * ws
+    value = total / (ms_max / 1e3) / 1e9
+
+    # roofline of the dominant kernel (algorithmic bytes / event time)
+    c = comp_bytes / nsym
+    table_bytes = {"push": push_t.numel() * 4 + 16 * push_t.shape[0], "pop": pop_t.numel() * 4 + 16 * pop_t.shape[0]}
+    alg = {"push": nsym * (8 + c) + table_bytes["push"], "pop": nsym * (8 + c) + table_bytes["pop"]}
+    dom = "pop" if pop_ms >= push_ms else "push"
+    dom_ms = pop_ms if dom == "pop" else push_ms
+    peak, peak_kind = measured_peak_hbm()
+    achieved = alg[dom] / (dom_ms / 1e3) / 1e9
+    traffic = None
+    try:
+        prof = json.load(open(os.path.join(ROOT, "profiles", "traffic.json")))
+        ent = prof.get(f"{args.workload}:{dom}")
+        if ent:
+            traffic = ent["dram_bytes_per_symbol"] * nsym
+    except Exception:
+        pass
+    res = dict(value=value, ms=ms_max, push_ms=push_ms_max, pop_ms=pop_ms_max, ok=all_ok, nsym=nsym, B=B, N=N,
+               comp_bytes_per_symbol=c, clocks=clk.summary(),
+               roofline={"bound": "hbm", "kernel": f"{w.pop_op if dom == 'pop' else w.push_op}",
+                         "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "peak_kind": peak_kind, "traffic": traffic,
+                         "algorithmic_bytes_per_launch": alg[dom], "launch_ms": dom_ms},
+               encode_gsym_s=total / (push_ms_max / 1e3) / 1e9, decode_gsym_s=total / (pop_ms_max / 1e3) / 1e9)
+    if not args.no_e2e:
+        res["e2e"] = run_e2e(args, w, ws, rank, dev, _C, push, pop, init_cpu, push_t, pop_t, kw)
+    del w
+    torch.cuda.empty_cache()
+    return res
+
+
+def run_e2e(args, w, ws, rank, dev, _C, push, pop, init_cpu, push_t, pop_t, kw):
+    """Round trip through the public API from pinned host memory (host wall clock)."""
+    B, N = w.symbols.shape
+    h_sym = torch.empty((B, N), dtype=torch.int32, pin_memory=True)
+    h_idx = torch.empty((B, N), dtype=torch.int32, pin_memory=True)
+    h_out = torch.empty((B, N), dtype=torch.int32, pin_memory=True)
+    h_sym.copy_(w.symbols)
+    h_idx.copy_(w.indexes)
+    torch.cuda.synchronize()
+    h2d = d2h = 0
+    pinned = {"buf": torch.empty(0, dtype=torch.uint8)}
+
+    def once():
+        nonlocal h2d, d2h
+        # encode side
+        sym = h_sym.to(dev, non_blocking=True)
+        idx = h_idx.to(dev, non_blocking=True)
+        st = init_cpu.to(dev, non_blocking=True)
+        push(st, sym, idx, push_t, w.cdfs_sizes, w.offsets, **kw)
+        del sym
+        packed = _C.stream_to_merged_tensor(st, 4, None)
+        del st
+        if ws > 1:  # place this rank's records in the job-wide bitstream
+            n_local = torch.tensor([packed.numel()], dtype=torch.int64, device=dev)
+            sizes = [torch.zeros_like(n_local) for _ in range(ws)]
+            dist.all_gather(sizes, n_local)
+        if pinned["buf"].numel() < packed.numel():
+            pinned["buf"] = torch.empty(int(packed.numel() * 1.05) + (1 << 20), dtype=torch.uint8, pin_memory=True)
+        h_packed = pinned["buf"][: packed.numel()]
+        h_packed.copy_(packed, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+        del packed
+        # decode side
+        idx = h_idx.to(dev, non_blocking=True)
+        st2 = _C.merged_tensor_to_stream(h_packed, 4, None, str(dev))
+        dec = pop(st2, idx, pop_t, w.cdfs_sizes, w.offsets, **kw)
+        h_out.copy_(dec, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+        h2d = 2 * B * N * 4 + B * N * 4 + h_packed.numel()
+        d2h = h_packed.numel() + B * N * 4
+        return h_packed.numel()
+
+    once()  # warm-up (pinned buffer allocation, table prep)
+    ok = bool(torch.equal(h_out, h_sym))
+    barrier(ws)
+    t = time.perf_counter()
+    for _ in range(args.e2e_steps):
+        once()
+    barrier(ws)
+    el = (time.perf_counter() - t) / args.e2e_steps
+    ok = ok and bool(torch.equal(h_out, h_sym))
+    el = max_over_ranks(el, ws)
+    all_ok = max_over_ranks(0.0 if ok else 1.0, ws) == 0.0
+    del h_sym, h_idx, h_out
+    return {"value": B * N * ws / el / 1e9, "unit": UNIT, "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
+            "ms_per_step": el * 1e3, "ok": all_ok,
+            "path": "pinned host -> _C push -> stream_to_merged_tensor -> host -> merged_tensor_to_stream -> _C pop -> host"}
+
+
+# ----------------------------------------------------------------------------- reference CPU
+def cpu_reference(workload_name, seconds, scale, length_scale, steps=1, warmup=0):
+    """Time the reference CPU implementation (oracle/_ref, else the oracle's C port) on a
+    bounded sample of the workload: S streams of the configuration (same tables, same stream
+    length), S chosen so one push + pop takes about `seconds` on all host threads."""
+    from oracle import build_ref
+    ref = build_ref.load()
+    kind = "reference" if ref is not None else "port"
+    threads = len(os.sched_getaffinity(0))
+    torch.set_num_threads(threads)
+    probe = build_workload(workload_name, "cpu", scale=scale, length_scale=length_scale)
+    b_full = probe.symbols.shape[0]
+    del probe
+
+    def make(nstreams):
+        return build_workload(workload_name, "cpu", scale=scale * nstreams / b_full, length_scale=length_scale)
+
+    def run(w):
+        B = w.symbols.shape[0]
+        push_t, pop_t = w.tables_for_push().contiguous(), w.tables_for_pop().contiguous()
+        kw = dict(freq_precision=w.fp, bypass_coding=w.bypass, bypass_precision=w.bp)
+        if kind == "reference":
+            st = getattr(ref, f"{w.variant}_init_stream")(B)
+            t0 = time.perf_counter()
+            getattr(ref, w.push_op)(st, w.symbols, w.indexes, push_t, w.cdfs_sizes, w.offsets, **kw)
+            t1 = time.perf_counter()
+            dec = getattr(ref, w.pop_op)(st, w.indexes, pop_t, w.cdfs_sizes, w.offsets, **kw)
+            t2 = time.perf_counter()
+        else:
+            from oracle import oracle as O
+            st = O.init_stream(w.variant, B)
+            t0 = time.perf_counter()
+            st, _ = O.push(w.variant, st, w.symbols.numpy(), w.indexes.numpy(), push_t.numpy(), w.cdfs_sizes.numpy(),
+                           w.offsets.numpy(), w.fp, w.bypass, w.bp, alias=w.lookup == "alias", threads=threads)
+            t1 = time.perf_counter()
+            dec, _ = O.pop(w.variant, st, w.indexes.numpy(), pop_t.numpy(), w.cdfs_sizes.numpy(), w.offsets.numpy(),
+                           w.fp, w.bypass, w.bp, lookup=w.lookup, threads=threads)
+            dec = torch.from_numpy(dec)
+            t2 = time.perf_counter()
+        assert torch.equal(dec, w.symbols), "reference CPU round trip failed"
+        return t1 - t0, t2 - t1
+
+    n = min(b_full, max(threads, 1))
+    w = make(n)
+    tp, tq = run(w)
+    per_stream = (tp + tq) / n
+    n2 = int(min(b_full, max(n, seconds / max(per_stream, 1e-9))))
+    if n2 >= threads:
+        n2 = n2 // threads * threads
+    if n2 > n:
+        del w
+        n = n2
+        w = make(n)
+    for _ in range(warmup):
+        run(w)
+    tps, tqs = [], []
+    for _ in range(max(1, steps)):
+        tp, tq = run(w)
+        tps.append(tp)
+        tqs.append(tq)
+    tp, tq = sum(tps) / len(tps), sum(tqs) / len(tqs)
+    N = w.symbols.shape[1]
+    nsym = n * N
+    return {"value": nsym / (tp + tq) / 1e9, "unit": UNIT, "cores": threads, "kind": kind,
+            "sample": f"{n} of {b_full} streams x {N} symbols ({nsym} symbols) of {workload_name}, push + pop",
+            "encode_gsym_s": nsym / tp / 1e9, "decode_gsym_s": nsym / tq / 1e9, "ms_per_step": (tp + tq) * 1e3}
+
+
+def main():
+    args = parse()
+    ws, rank, local = dist_setup()
+    cfg = {"workload": args.workload, "scale": args.scale, "length_scale": args.length_scale,
+           "l2": "inputs larger than L2 (no flush)", "parallelism": f"stream shards x{ws}" if ws > 1 else "single GPU"}
+    if args.impl == "reference":
+        if rank == 0:
+            per_step = max(2.0, 150.0 / max(1, args.steps + args.warmup))
+            base = cpu_reference(args.workload, per_step, args.scale, args.length_scale, steps=args.steps,
+                                 warmup=args.warmup)
+            line = {"metric": METRIC, "value": base["value"], "unit": UNIT, "n_gpus": ws, "steps": args.steps,
+                    "warmup": args.warmup, "ms_per_step": base["ms_per_step"], "higher_is_better": True, "scaling": "weak",
+                    "vs_baseline": None, "dtype": "int64", "data": "synthetic", "config": cfg, "impl": "reference",
+                    "cpu_baseline": base,
+                    "e2e": {"value": base["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+            print(json.dumps(line), flush=True)
+        if ws > 1:
+            dist.destroy_process_group()
+        return
+
+    res = run_ours(args, ws, rank, local)
+    base = None
+    if rank == 0 and ws == 1 and not args.no_cpu:
+        base = cpu_reference(args.workload, args.cpu_seconds, args.scale, args.length_scale)
+    if rank == 0:
+        cfg.update({"streams_per_gpu": res["B"], "symbols_per_stream": res["N"], "global_batch_streams": res["B"] * ws,
+                    "compressed_bytes_per_symbol": round(res["comp_bytes_per_symbol"], 4)})
+        line = {"metric": METRIC, "value": res["value"], "unit": UNIT, "n_gpus": ws, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": res["ms"], "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "int64", "data": "synthetic", "config": cfg,
+                "encode_gsym_s": res["encode_gsym_s"], "decode_gsym_s": res["decode_gsym_s"],
+                "push_ms": res["push_ms"], "pop_ms": res["pop_ms"], "bit_exact_roundtrip": res["ok"],
+                "roofline": res["roofline"], "clocks": res["clocks"],
+                "gpu_launches": args.steps * 6, "cpu_baseline": base}
+        if "e2e" in res:
+            line["e2e"] = res["e2e"]
+        print(json.dumps(line), flush=True)
+    if ws > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

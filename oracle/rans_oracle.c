@@ -86,6 +86,7 @@ typedef struct {
   int64_t cap_words;  /* words that fit in the row's payload */
   int64_t first_word; /* first word index after the state slots */
   uint32_t err;
+  int last_ok;        /* whether the last orc_pop_step decoded a symbol (0 when it was skipped) */
 } orc_cursor;
 
 static inline uint64_t orc_read_word(const orc_cursor* c, int64_t j) {
@@ -189,15 +190,15 @@ static int32_t orc_pop_raw(orc_cursor* c, uint64_t* xs, int bp) {
   x >>= bp;
   orc_pop_renorm(c, &x);
   int32_t n = val;
-  while (val == maxb) {
+  /* a valid escape has at most 32 chunks; longer counts only come from corrupt streams */
+  while (val == maxb && n <= 32) {
     val = (int32_t)(x & (uint64_t)((1u << bp) - 1));
     x >>= bp;
     orc_pop_renorm(c, &x);
     n += val;
-    if ((int64_t)n * bp > 32) break;
   }
   int32_t raw = 0;
-  if ((int64_t)n * bp > 32) { c->err |= ORC_ERR_BAD_ESCAPE; n = 0; }
+  if (n > 32) { c->err |= ORC_ERR_BAD_ESCAPE; n = 0; }
   for (int j = 0; j < n; ++j) {
     val = (int32_t)(x & (uint64_t)((1u << bp) - 1));
     x >>= bp;
@@ -214,6 +215,7 @@ static int32_t orc_pop_step(orc_cursor* c, uint64_t* xs, const int32_t* cdf, int
                             int32_t offset, int fp, int bypass, int bp, int lookup) {
   const orc_variant* v = c->v;
   const int32_t maxv = cdf_size - 2;
+  c->last_ok = 0;
   uint64_t x = *xs;
   const int32_t cum = (int32_t)(x & ((1ull << fp) - 1));
   int64_t s;
@@ -250,6 +252,7 @@ static int32_t orc_pop_step(orc_cursor* c, uint64_t* xs, const int32_t* cdf, int
   x = (((x >> fp) * orc_to_state(v, freq)) + orc_to_state(v, cum_off)) & v->state_mask;
   orc_pop_renorm(c, &x);
   *xs = x;
+  c->last_ok = 1;
   if (bypass && value == maxv) {
     const int32_t raw = orc_pop_raw(c, xs, bp);
     value = raw >> 1;
@@ -399,15 +402,18 @@ uint32_t orc_pop(int variant, int lookup, int interleave, int32_t* stream, int64
         continue;
       }
       /* rans_cpu.cpp:236-278: four symbol pops (state j), then the escapes of the block */
+      int okj[4];
       for (int j = 0; j < I; j++) {
         const int32_t* row_c; int32_t sz, off;
+        okj[j] = 0;
         if (!orc_table(&t, idx[i + j], &row_c, &sz, &off)) { c.err |= ORC_ERR_BAD_INDEX; o[i + j] = 0; continue; }
         o[i + j] = orc_pop_step(&c, &st[j], row_c, sz, off, fp, 0, bp, lookup);
+        okj[j] = c.last_ok;
       }
       if (bypass) {
         for (int j = 0; j < I; j++) {
           const int32_t* row_c; int32_t sz, off;
-          if (!orc_table(&t, idx[i + j], &row_c, &sz, &off)) continue;
+          if (!okj[j] || !orc_table(&t, idx[i + j], &row_c, &sz, &off)) continue;
           const int32_t maxv = sz - 2;
           int32_t value = (int32_t)((uint32_t)o[i + j] - (uint32_t)off);
           if (value == maxv) {

@@ -1,0 +1,264 @@
+"""GPU parity tests: the CUDA coding path against the reference's golden vectors and the oracle.
+
+Bar: bit-exact.  Every pushed stream must have the reference's row width, length column and
+payload bytes; every pop must return the identical int32 symbols and leave the identical row
+length and state.  Paths covered: the `_C` op surface (what the reference's callers bind) and the
+raw C ABI through ctypes (what a non-torch host binds).
+"""
+import zlib
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as O
+from tests import golden_cases as G
+
+pytestmark = pytest.mark.gpu
+
+VARIANTS = ["rans64", "rans32", "rans32_16"]
+FP = {"rans64": 16, "rans32": 16, "rans32_16": 15}
+
+
+@pytest.fixture(scope="module")
+def C():
+    from torch_ans_b200 import _C
+    _C.set_sync_check(False)
+    _C.device_status(reset=True)
+    return _C
+
+
+def op_names(variant, interleave, alias_push, lookup):
+    if interleave == 4:
+        push = f"{variant}_i4_push"
+        pop = f"{variant}_i4_invcdf_pop" if lookup == "invcdf" else f"{variant}_i4_pop"
+    else:
+        push = f"{variant}_alias_push" if alias_push else f"{variant}_push"
+        pop = {"alias": f"{variant}_alias_pop", "invcdf": f"{variant}_invcdf_pop", "search": f"{variant}_pop"}[lookup]
+    return push, pop
+
+
+def same_rows(a, b):
+    a, b = np.asarray(a), np.asarray(b)
+    return a.shape == b.shape and np.array_equal(a[:, 0], b[:, 0]) and G.payload_bytes(a) == G.payload_bytes(b)
+
+
+def t(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+@pytest.mark.parametrize("name", G.coding_cases())
+def test_golden_through_op_surface(C, name):
+    d = G.load(name)
+    m = d["meta"]
+    push, pop = op_names(m["variant"], m["interleave"], m["alias_push"], m["lookup"])
+    kw = dict(freq_precision=m["fp"], bypass_coding=bool(m["bypass"]), bypass_precision=m["bp"])
+    stream = t(d["stream_in"])
+    getattr(C, push)(stream, t(d["symbols"]), t(d["indexes"]), t(d["push_cdfs"]), t(d["sizes"]), t(d["offsets"]), **kw)
+    assert C.device_status() == 0
+    got = stream.cpu().numpy()
+    assert got.shape == d["pushed"].shape
+    assert np.array_equal(got[:, 0], d["pushed"][:, 0])
+    assert G.payload_bytes(got) == d["pushed_bytes"].tobytes()
+    assert b"".join(C.rans_stream_to_byte_strings(stream)) == d["pushed_bytes"].tobytes()
+    st2 = C.rans_byte_strings_to_stream(C.rans_stream_to_byte_strings(stream)).cuda()
+    dec = getattr(C, pop)(st2, t(d["indexes"]), t(d["pop_cdfs"]), t(d["sizes"]), t(d["offsets"]), **kw)
+    assert C.device_status() == 0
+    assert np.array_equal(dec.cpu().numpy(), d["decoded"])
+    assert same_rows(st2.cpu().numpy(), d["popped"])
+
+
+@pytest.mark.parametrize("name", [n for n in G.coding_cases() if "i4" not in n][::2])
+def test_golden_through_c_abi(name):
+    """Same golden cases, calling libtorch_ans_b200 directly with device pointers (ctypes)."""
+    from torch_ans_b200 import capi
+    lib = capi.load()
+    d = G.load(name)
+    m = d["meta"]
+    v = capi.VARIANT[m["variant"]]
+    W = O.resized_width(d["stream_in"], d["symbols"].shape[1], m["fp"], bool(m["bypass"]))
+    host = np.zeros((d["stream_in"].shape[0], W), np.int32)
+    host[:, : d["stream_in"].shape[1]] = d["stream_in"]
+    stream = t(host)
+    sym, idx, pc, sz, off = t(d["symbols"]), t(d["indexes"]), t(d["push_cdfs"]), t(d["sizes"]), t(d["offsets"])
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    cs = torch.cuda.current_stream().cuda_stream
+    B, N = sym.shape
+    K, Wc = pc.shape
+    ws_bytes = lib.tans_push_workspace_size(v, K, Wc)
+    ws = torch.empty(ws_bytes + 256, dtype=torch.uint8, device="cuda")
+    rc = lib.tans_push(v, int(m["alias_push"]), 1, stream.data_ptr(), B, W, sym.data_ptr(), idx.data_ptr(), N,
+                       pc.data_ptr(), K, Wc, sz.data_ptr(), off.data_ptr(), m["fp"], m["bypass"], m["bp"],
+                       ws.data_ptr(), ws.numel(), status.data_ptr(), cs)
+    assert rc == 0
+    torch.cuda.synchronize()
+    assert status.item() == 0
+    got = stream.cpu().numpy()
+    assert np.array_equal(got[:, 0], d["pushed"][:, 0]) and G.payload_bytes(got) == d["pushed_bytes"].tobytes()
+    # pop with the library allocating its own scratch (workspace = NULL)
+    qc = t(d["pop_cdfs"])
+    out = torch.empty_like(idx)
+    rc = lib.tans_pop(v, capi.LOOKUP[m["lookup"]], 1, stream.data_ptr(), B, W, out.data_ptr(), idx.data_ptr(), N,
+                      qc.data_ptr(), qc.shape[0], qc.shape[1], sz.data_ptr(), off.data_ptr(), m["fp"], m["bypass"],
+                      m["bp"], None, 0, status.data_ptr(), cs)
+    assert rc == 0
+    torch.cuda.synchronize()
+    assert status.item() == 0
+    assert np.array_equal(out.cpu().numpy(), d["decoded"])
+    assert same_rows(stream.cpu().numpy(), d["popped"])
+
+
+@pytest.mark.parametrize("variant", VARIANTS)
+def test_streaming_pushes_and_partial_pops(C, variant):
+    d = G.load(f"{variant}_streaming")
+    fp = d["meta"]["fp"]
+    cdfs, sizes, offs = t(d["cdfs"]), t(d["sizes"]), t(d["offsets"])
+    st = getattr(C, f"{variant}_init_stream")(3).cuda()
+    push, pop = getattr(C, f"{variant}_push"), getattr(C, f"{variant}_pop")
+    push(st, t(d["s2"]), t(d["i2"]), cdfs, sizes, offs, freq_precision=fp)
+    assert same_rows(st.cpu().numpy(), d["after1"])
+    push(st, t(d["s1"]), t(d["i1"]), cdfs, sizes, offs, freq_precision=fp)
+    assert same_rows(st.cpu().numpy(), d["after2"])
+    d1 = pop(st, t(d["i1"]), cdfs, sizes, offs, freq_precision=fp)
+    assert np.array_equal(d1.cpu().numpy(), d["s1"]) and same_rows(st.cpu().numpy(), d["mid"])
+    d2 = pop(st, t(d["i2"]), cdfs, sizes, offs, freq_precision=fp)
+    assert np.array_equal(d2.cpu().numpy(), d["s2"]) and same_rows(st.cpu().numpy(), d["final"])
+    assert C.device_status() == 0
+
+
+def _random_case(rng, variant, bypass, K=5, A=40):
+    fp = FP[variant]
+    pm = rng.integers(1, 1024, (K, A)).astype(np.float32)
+    pm = np.concatenate([pm, np.ones((K, 1), np.float32)], 1)
+    pm /= pm.sum(1, keepdims=True)
+    cdfs = O.pmf_to_quantized_cdf(pm, fp)
+    sizes = np.full(K, A + 2, np.int32)
+    offs = rng.integers(-8, 8, K).astype(np.int32)
+    return fp, cdfs, sizes, offs
+
+
+@pytest.mark.parametrize("variant", VARIANTS)
+@pytest.mark.parametrize("bypass", [False, True])
+@pytest.mark.parametrize("interleave", [1, 4])
+@pytest.mark.parametrize("lookup", ["search", "invcdf", "alias"])
+def test_random_against_oracle(C, variant, bypass, interleave, lookup):
+    """Seeded cases with odd lengths and misaligned rows (vector and scalar load paths)."""
+    if lookup == "alias" and interleave == 4:
+        pytest.skip("the reference has no 4-state alias op")
+    if lookup == "invcdf" and interleave == 4 and variant == "rans64":
+        pytest.skip("the reference has no rans64_i4_invcdf_pop")
+    rng = np.random.default_rng(zlib.crc32(f"{variant}-{bypass}-{interleave}-{lookup}".encode()))
+    if lookup == "alias":
+        fp = 12
+        K, sp = 3, 5
+        A = 1 << sp  # cdf_size - 1 must equal the 2^sp alias cuts; with escapes the last slot is the escape
+        pm = rng.random((K, A)) + 0.05
+        cdfs = O.pmf_to_quantized_cdf((pm / pm.sum(1, keepdims=True)).astype(np.float32), fp)
+        sizes = np.full(K, A + 1, np.int32)
+        offs = rng.integers(-3, 3, K).astype(np.int32)
+        push_c, pop_c, ok = O.alias_build_table(cdfs, sizes, sp, fp)
+        assert ok == K
+        lo, hi = (-5, A + 5) if bypass else (0, A)
+    else:
+        fp, cdfs, sizes, offs = _random_case(rng, variant, bypass)
+        push_c = cdfs
+        pop_c = np.concatenate([cdfs, O.inverse_quantized_cdf(cdfs, fp)], 1) if lookup == "invcdf" else cdfs
+        A = cdfs.shape[1] - 2
+        lo, hi = (-20, A + 20) if bypass else (0, A + 1)
+    K = cdfs.shape[0]
+    B, N = 37, 1001
+    idx = rng.integers(0, K, (B, N)).astype(np.int32)
+    sym = (rng.integers(lo, hi, (B, N)) + (offs[idx] if not bypass else 0)).astype(np.int32)
+    if not bypass:
+        sym = np.clip(sym - offs[idx], 0, sizes[idx] - 2) + offs[idx]
+        sym = sym.astype(np.int32)
+    ref_stream, perr = O.push(variant, O.init_stream(variant, B, interleave), sym, idx, push_c, sizes, offs, fp, bypass,
+                              4, alias=(lookup == "alias"), interleave=interleave)
+    assert perr == 0
+    ref_pop_stream = ref_stream.copy()
+    ref_dec, derr = O.pop(variant, ref_pop_stream, idx, pop_c, sizes, offs, fp, bypass, 4, lookup=lookup,
+                          interleave=interleave)
+    assert derr == 0 and np.array_equal(ref_dec, sym)
+    push, pop = op_names(variant, interleave, lookup == "alias", lookup)
+    # misaligned inputs: views one element into bigger buffers force the scalar load path
+    for misalign in (0, 1):
+        big_s = torch.zeros(B * N + 1, dtype=torch.int32, device="cuda")
+        big_i = torch.zeros(B * N + 1, dtype=torch.int32, device="cuda")
+        big_s[misalign:misalign + B * N] = t(sym).reshape(-1)
+        big_i[misalign:misalign + B * N] = t(idx).reshape(-1)
+        s_in = big_s[misalign:misalign + B * N].view(B, N)
+        i_in = big_i[misalign:misalign + B * N].view(B, N)
+        st = getattr(C, f"{variant}_init_stream")(B, interleave).cuda()
+        kw = dict(freq_precision=fp, bypass_coding=bypass, bypass_precision=4)
+        getattr(C, push)(st, s_in, i_in, t(push_c), t(sizes), t(offs), **kw)
+        assert C.device_status() == 0
+        assert same_rows(st.cpu().numpy(), ref_stream)
+        dec = getattr(C, pop)(st, i_in, t(pop_c), t(sizes), t(offs), **kw)
+        assert C.device_status() == 0
+        assert np.array_equal(dec.cpu().numpy(), sym)
+        assert same_rows(st.cpu().numpy(), ref_pop_stream)
+
+
+@pytest.mark.parametrize("variant", VARIANTS)
+def test_error_bits_match_oracle(C, variant):
+    """Invalid table indexes and out-of-range symbols are flagged, not read out of bounds."""
+    fp = FP[variant]
+    cdfs = np.array([[0, 10, 20, 1 << fp]], np.int32)
+    sizes = np.array([4], np.int32)
+    sym = np.array([[0, 5, 1, 2, 0]], np.int32)
+    idx = np.array([[0, 0, 3, 0, -1]], np.int32)
+    ref, err = O.push(variant, O.init_stream(variant, 1), sym, idx, cdfs, sizes, None, fp, False)
+    st = getattr(C, f"{variant}_init_stream")(1).cuda()
+    getattr(C, f"{variant}_push")(st, t(sym), t(idx), t(cdfs), t(sizes), freq_precision=fp, bypass_coding=False)
+    bits = C.device_status()
+    assert bits == err and bits & O.ERR_BAD_INDEX and bits & O.ERR_BAD_VALUE
+    assert same_rows(st.cpu().numpy(), ref)
+    C.set_sync_check(True)
+    try:
+        with pytest.raises(RuntimeError, match="table-index-out-of-range"):
+            getattr(C, f"{variant}_push")(st, t(sym), t(idx), t(cdfs), t(sizes), freq_precision=fp, bypass_coding=False)
+    finally:
+        C.set_sync_check(False)
+    C.device_status()
+
+
+def test_pmf_to_quantized_cdf_on_gpu_matches_reference(C):
+    d = G.load("pmf_to_quantized_cdf")
+    for p in (8, 12, 16):
+        got = C.rans_pmf_to_quantized_cdf(t(d["pmf"]), p)
+        assert got.is_cuda and np.array_equal(got.cpu().numpy(), d[f"cdf{p}"])
+    assert C.rans_pmf_to_quantized_cdf(torch.tensor([0.25] * 4).cuda(), 8).tolist() == [0, 64, 128, 192, 256]
+    assert C.rans_pmf_to_quantized_cdf(torch.tensor([0.1, 0.2, 0.3, 0.4]).cuda(), 8).tolist() == [0, 26, 77, 154, 256]
+    # a CPU pmf is computed on the GPU and returned on the CPU
+    assert C.rans_pmf_to_quantized_cdf(torch.tensor([0.1, 0.2, 0.3, 0.4]), 8).device.type == "cpu"
+
+
+def test_device_stream_helpers():
+    from torch_ans_b200 import capi
+    lib = capi.load()
+    cs = torch.cuda.current_stream().cuda_stream
+    for variant, ilv in (("rans64", 1), ("rans32", 4), ("rans32_16", 4)):
+        W = 1 + ilv * (8 if variant == "rans64" else 4) // 4 + 5
+        s = torch.full((6, W), 7, dtype=torch.int32, device="cuda")
+        assert lib.tans_init_stream(capi.VARIANT[variant], ilv, s.data_ptr(), 6, W, cs) == 0
+        ref = np.zeros((6, W), np.int32)
+        ref[:, : O.init_stream(variant, 6, ilv).shape[1]] = O.init_stream(variant, 6, ilv)
+        assert np.array_equal(s.cpu().numpy(), ref)
+    d = G.load("rans32_bypass")
+    st = t(d["pushed"])
+    segs = O.stream_to_byte_strings(d["pushed"])
+    mx = torch.zeros(1, dtype=torch.int32, device="cuda")
+    assert lib.tans_stream_max_length(st.data_ptr(), st.shape[0], st.shape[1], mx.data_ptr(), cs) == 0
+    assert mx.item() == max(len(x) for x in segs)
+    from torch_ans_b200 import _C
+    for nb in (1, 2, 4, 8):
+        for ns in (None, len(segs)):
+            assert _C.stream_to_merged_bytes(st, nb, ns) == O.merge_bytes(segs, nb, ns)
+    # scatter back
+    lens = torch.tensor([len(x) for x in segs], dtype=torch.int32, device="cuda")
+    offs = torch.tensor(np.concatenate([[0], np.cumsum([len(x) for x in segs])[:-1]]), dtype=torch.int64, device="cuda")
+    flat = torch.tensor(np.frombuffer(b"".join(segs), np.uint8).copy(), device="cuda")
+    out = torch.full_like(st, -1)
+    assert lib.tans_scatter_payloads(flat.data_ptr(), offs.data_ptr(), lens.data_ptr(), out.data_ptr(), st.shape[0],
+                                     st.shape[1], cs) == 0
+    assert same_rows(out.cpu().numpy(), d["pushed"])

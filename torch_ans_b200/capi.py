@@ -1,0 +1,65 @@
+"""ctypes binding of the C ABI library ``libtorch_ans_b200.so`` (include/torch_ans_b200.h).
+
+This is the binding a non-torch host (or a test) uses: plain device pointers, sizes and a CUDA
+stream handle.  ``SYMBOLS`` lists every entry point the header declares.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+
+LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libtorch_ans_b200.so")
+HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include", "torch_ans_b200.h")
+
+RANS64, RANS32, RANS32_16 = 0, 1, 2
+LOOKUP_SEARCH, LOOKUP_INVCDF, LOOKUP_ALIAS = 0, 1, 2
+VARIANT = {"rans64": RANS64, "rans32": RANS32, "rans32_16": RANS32_16}
+LOOKUP = {"search": LOOKUP_SEARCH, "invcdf": LOOKUP_INVCDF, "alias": LOOKUP_ALIAS}
+
+OK = 0
+DEV_BAD_INDEX, DEV_BAD_VALUE, DEV_OVERFLOW, DEV_UNDERFLOW, DEV_BAD_FREQ, DEV_BAD_ESCAPE = 1, 2, 4, 8, 16, 32
+
+_P, _I64, _I, _SZ = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_size_t
+_SIGS = {
+    "tans_version": ([], _I),
+    "tans_status_string": ([_I], ctypes.c_char_p),
+    "tans_push_workspace_size": ([_I, _I64, _I64], _SZ),
+    "tans_push": ([_I, _I, _I, _P, _I64, _I64, _P, _P, _I64, _P, _I64, _I64, _P, _P, _I, _I, _I, _P, _SZ, _P, _P], _I),
+    "tans_pop_workspace_size": ([_I, _I, _I64, _I64, _I], _SZ),
+    "tans_pop": ([_I, _I, _I, _P, _I64, _I64, _P, _P, _I64, _P, _I64, _I64, _P, _P, _I, _I, _I, _P, _SZ, _P, _P], _I),
+    "tans_stream_max_length": ([_P, _I64, _I64, _P, _P], _I),
+    "tans_init_stream": ([_I, _I, _P, _I64, _I64, _P], _I),
+    "tans_gather_payloads": ([_P, _I64, _I64, _P, _I, _I64, _P, _P], _I),
+    "tans_scatter_payloads": ([_P, _P, _P, _P, _I64, _I64, _P], _I),
+    "tans_cdf_fix_zero_freqs": ([_P, _I64, _I64, _P, _P], _I),
+}
+
+_lib = None
+
+
+def declared_symbols(header: str = HEADER):
+    """Names of the functions declared in the C header."""
+    text = open(header).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(tans_\w+)\s*\(", text)))
+
+
+def load():
+    """Load libtorch_ans_b200.so and set argument types of every declared entry point."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise OSError(f"{LIB_PATH} is not built; run `python -m torch_ans_b200.build`")
+        lib = ctypes.CDLL(LIB_PATH)
+        for name, (args, res) in _SIGS.items():
+            f = getattr(lib, name, None)
+            if f is not None:
+                f.argtypes = args
+                f.restype = res
+        _lib = lib
+    return _lib
+
+
+def ptr(t) -> int:
+    return t.data_ptr() if t is not None else None

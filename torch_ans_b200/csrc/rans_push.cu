@@ -1,0 +1,449 @@
+// rans_push.cu -- encode (push) kernels and the tans_push C entry point.
+//
+// Replaces the reference's rans_push_indexed_cpu / rans_push_indexed_cuda
+// (torch_ans/rans_cpu.cpp:44-189, torch_ans/rans_cuda.cu:20-167): per stream, symbols are pushed
+// last-first onto the stream row with the step of torch_ans/rans_utils.hpp:168-323.
+//
+// B200 design:
+//  * one thread per stream (launch.cuh spreads streams over all SMs);
+//  * a per-call prep kernel turns every (table, symbol) of the cdf list into a 16-byte entry
+//    {reciprocal, freq, start}, so the serial chain of a step is compare/emit + multiply-high
+//    + multiply-add instead of a 64-bit division (rans_device.cuh);
+//  * symbol/index rows are read with 16-byte vector loads four chunks (16 symbols) ahead of the
+//    chain, and table entries two chunks ahead, so no memory latency sits on the chain except
+//    the alias remap lookup, which is part of the algorithm.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+
+#include "../../include/torch_ans_b200.h"
+#include "launch.cuh"
+#include "rans_device.cuh"
+#include "rans_host.h"
+
+namespace tans {
+
+struct PushParams {
+  int32_t* stream;
+  int64_t batch, width;
+  const int32_t* sym;
+  const int32_t* idx;
+  int64_t nsym;
+  const uint4* enc;
+  int64_t enc_stride;
+  const TableInfo* tinfo;
+  int64_t ntables;
+  const int32_t* cdfs;
+  int64_t cdf_width;
+  int fp, bp;
+  uint32_t* status;
+  int lanes;
+  int vec;
+};
+
+// ---------------------------------------------------------------- prep: table info + entries
+__global__ void build_table_info_kernel(const int32_t* sizes, const int32_t* offsets, int64_t ntables,
+                                        int fp, TableInfo* out) {
+  for (int64_t k = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; k < ntables;
+       k += (int64_t)gridDim.x * blockDim.x) {
+    TableInfo t;
+    t.size = sizes[k];
+    t.offset = offsets ? offsets[k] : 0;
+    // alias cut width of rans_utils.hpp:413: (1 << fp) / (cdf_size - 1); 0 marks "unusable"
+    t.cut = (t.size - 1 > 0) ? (int32_t)((1 << fp) / (t.size - 1)) : 0;
+    t.cut_log2 = (t.cut > 0 && (t.cut & (t.cut - 1)) == 0) ? (31 - __clz(t.cut)) : -1;
+    out[k] = t;
+  }
+}
+
+template <int V>
+__global__ void build_push_entries_kernel(const int32_t* cdfs, int64_t ntables, int64_t cdf_width,
+                                          int64_t stride, uint4* enc) {
+  const int64_t total = ntables * stride;
+  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t k = e / stride, v = e - k * stride;
+    const int32_t* row = cdfs + k * cdf_width;
+    const int32_t start = row[v];
+    const int32_t freq = (int32_t)((uint32_t)row[v + 1] - (uint32_t)start);
+    uint4 out;
+    out.w = (uint32_t)start;
+    if (freq <= 0) {
+      out.x = out.y = out.z = 0u;
+    } else {
+      const uint32_t d = (uint32_t)freq;
+      out.z = d;
+      if constexpr (V == 0) {
+        const unsigned long long m = d > 1u ? recip64(d) : 0ull;
+        out.x = (uint32_t)m;
+        out.y = (uint32_t)(m >> 32);
+      } else {
+        out.x = d > 1u ? recip32(d) : 0u;
+        out.y = 0u;
+      }
+    }
+    enc[e] = out;
+  }
+}
+
+// ---------------------------------------------------------------- step pieces
+template <int V> struct PushCursor {
+  uint8_t* payload;  // row + 1
+  int64_t p;         // index of the last written word
+  int64_t cap;       // words that fit in the row
+  uint32_t err;
+
+  __device__ __forceinline__ void emit(typename VT<V>::State& x) {
+    using W = typename VT<V>::Word;
+    p += 1;
+    if (p >= 0 && p < cap) reinterpret_cast<W*>(payload)[p] = (W)x;
+    else err |= DEV_OVERFLOW;
+    x >>= VT<V>::WB;
+  }
+};
+
+// RANS_APPEND_BITS, rans_utils.hpp:63-68
+template <int V>
+__device__ __forceinline__ void append_bits(typename VT<V>::State& x, PushCursor<V>& c, int32_t value, int nbits) {
+  using S = typename VT<V>::State;
+  const unsigned long long bound = (VT<V>::LB >> nbits) << VT<V>::WB;
+#pragma unroll
+  for (int t = 0; t < VT<V>::MAX_RENORM; ++t)
+    if ((unsigned long long)x >= bound) c.emit(x);
+  x = (S)((x << nbits) | to_state<S>(value));
+}
+
+__device__ __forceinline__ int32_t shr_defined(int32_t a, int n) { return n >= 32 ? (a < 0 ? -1 : 0) : (a >> n); }
+
+// rans_push_raw_value_step, rans_utils.hpp:106-164 (escape value, rare path)
+template <int V>
+__device__ __noinline__ void push_escape(typename VT<V>::State& x, PushCursor<V>& c, int32_t raw, int bp) {
+  const int32_t maxb = (int32_t)((1u << bp) - 1u);
+  int32_t nb = 0;
+  while (nb <= 32 && shr_defined(raw, nb * bp) != 0) ++nb;
+  const int32_t ncodes = nb / maxb;
+  const int32_t rest = nb - ncodes * maxb;
+  for (int32_t j = nb - 1; j >= 0; --j) append_bits<V>(x, c, shr_defined(raw, j * bp) & maxb, bp);
+  append_bits<V>(x, c, rest, bp);
+  for (int32_t j = 0; j < ncodes; ++j) append_bits<V>(x, c, maxb, bp);
+}
+
+enum : uint32_t { PREP_SKIP = 1u, PREP_ESC = 2u };
+
+struct PushPrep {
+  uint4 e;           // encode entry (in flight while the previous chunk runs)
+  int64_t rbase;     // alias: index of the remap row start (k * cdf_width + cdf_size)
+  int32_t rcap;      // alias: remap entries available in the row
+  int32_t raw;       // escape value
+  uint32_t flags;
+};
+
+template <int V, bool ALIAS, bool BYPASS>
+__device__ __forceinline__ PushPrep push_prepare(const PushParams& P, int32_t s, int32_t k, bool in_row,
+                                                 uint32_t& err) {
+  PushPrep r;
+  r.flags = PREP_SKIP;
+  r.raw = 0;
+  r.rbase = 0;
+  r.rcap = 0;
+  r.e = make_uint4(0, 0, 0, 0);
+  if (!in_row) return r;
+  if (k < 0 || (int64_t)k >= P.ntables) {
+    err |= DEV_BAD_INDEX;
+    return r;
+  }
+  const TableInfo t = load_tinfo(P.tinfo, k);
+  int32_t v = (int32_t)((uint32_t)s - (uint32_t)t.offset);
+  const int32_t maxv = t.size - 2;
+  uint32_t flags = 0;
+  if constexpr (BYPASS) {
+    if (v < 0) {
+      r.raw = -2 * v - 1;
+      v = maxv;
+    } else if (v >= maxv) {
+      r.raw = 2 * (v - maxv);
+      v = maxv;
+    }
+    if (v == maxv) flags |= PREP_ESC;
+  }
+  if (v < 0 || v >= t.size - 1 || (int64_t)v >= P.enc_stride) {
+    err |= DEV_BAD_VALUE;
+    return r;
+  }
+  r.e = __ldg(P.enc + (int64_t)k * P.enc_stride + v);
+  if constexpr (ALIAS) {
+    r.rbase = (int64_t)k * P.cdf_width + t.size;
+    const int64_t cap = P.cdf_width - t.size;
+    r.rcap = cap <= 0 ? 0 : (cap > 0x7fffffff ? 0x7fffffff : (int32_t)cap);
+  }
+  r.flags = flags;
+  return r;
+}
+
+// one symbol: escape (if any), renormalise, x = C(s, x)  (rans_utils.hpp:209-321)
+template <int V, bool ALIAS, bool BYPASS>
+__device__ __forceinline__ void push_chain(const PushParams& P, typename VT<V>::State& x, PushCursor<V>& c,
+                                           const PushPrep& r) {
+  using S = typename VT<V>::State;
+  if (r.flags & PREP_SKIP) return;
+  if constexpr (BYPASS) {
+    if (r.flags & PREP_ESC) push_escape<V>(x, c, r.raw, P.bp);
+  }
+  const uint32_t freq = r.e.z;
+  if (freq == 0u) {
+    c.err |= DEV_BAD_FREQ;
+    return;
+  }
+  const unsigned long long bound = (unsigned long long)freq << (VT<V>::USED - P.fp);
+#pragma unroll
+  for (int t = 0; t < VT<V>::MAX_RENORM; ++t)
+    if ((unsigned long long)x >= bound) c.emit(x);
+  const S q = quotient<V>(x, r.e);
+  const S start = to_state<S>((int32_t)r.e.w);
+  if constexpr (ALIAS) {
+    const S ri = (S)(x - q * (S)freq + start);
+    if ((unsigned long long)ri >= (unsigned long long)r.rcap) {
+      c.err |= DEV_BAD_VALUE;
+      return;
+    }
+    const int32_t rv = __ldg(P.cdfs + r.rbase + (int64_t)ri);
+    x = (S)((q << P.fp) + to_state<S>(rv));
+  } else {
+    const S cmpl = (S)((S)1 << P.fp) - (S)freq;
+    x = (S)(x + start + q * cmpl);
+  }
+}
+
+__device__ __forceinline__ int4 load_chunk(const int32_t* a, int64_t c, int64_t lo, int64_t hi, bool vec) {
+  const int64_t g = c * 4;
+  if (vec && g >= lo && g + 4 <= hi) return __ldg(reinterpret_cast<const int4*>(a) + c);
+  int4 r = make_int4(0, 0, 0, 0);
+  if (g >= lo && g < hi) r.x = __ldg(a + g);
+  if (g + 1 >= lo && g + 1 < hi) r.y = __ldg(a + g + 1);
+  if (g + 2 >= lo && g + 2 < hi) r.z = __ldg(a + g + 2);
+  if (g + 3 >= lo && g + 3 < hi) r.w = __ldg(a + g + 3);
+  return r;
+}
+
+template <int V, bool ALIAS, bool BYPASS>
+__device__ __forceinline__ void prep_chunk(const PushParams& P, int64_t c, int4 s4, int4 k4, int64_t lo, int64_t hi,
+                                           PushPrep (&out)[4], uint32_t& err) {
+  const int64_t g = c * 4;
+  out[0] = push_prepare<V, ALIAS, BYPASS>(P, s4.x, k4.x, g >= lo && g < hi, err);
+  out[1] = push_prepare<V, ALIAS, BYPASS>(P, s4.y, k4.y, g + 1 >= lo && g + 1 < hi, err);
+  out[2] = push_prepare<V, ALIAS, BYPASS>(P, s4.z, k4.z, g + 2 >= lo && g + 2 < hi, err);
+  out[3] = push_prepare<V, ALIAS, BYPASS>(P, s4.w, k4.w, g + 3 >= lo && g + 3 < hi, err);
+}
+
+// ---------------------------------------------------------------- single-state kernel
+template <int V, bool ALIAS, bool BYPASS>
+__global__ void __launch_bounds__(256) push_i1_kernel(const PushParams P) {
+  using S = typename VT<V>::State;
+  const int64_t b = my_stream(P.lanes, P.batch);
+  if (b < 0) return;
+  int32_t* row = P.stream + b * P.width;
+  PushCursor<V> cur;
+  cur.payload = reinterpret_cast<uint8_t*>(row + 1);
+  cur.p = (int64_t)row[0] / VT<V>::WBYTES - 1;
+  cur.cap = (P.width - 1) * 4 / VT<V>::WBYTES;
+  cur.err = 0;
+  S x = load_state<V>(row, 0);
+  uint32_t perr = 0;
+
+  const int64_t lo = b * P.nsym, hi = lo + P.nsym;
+  if (P.nsym > 0) {
+    const int64_t c_hi = (hi - 1) >> 2, c_lo = lo >> 2;
+    const bool vec = P.vec != 0;
+    PushPrep P0[4], P1[4], P2[4];
+    prep_chunk<V, ALIAS, BYPASS>(P, c_hi, load_chunk(P.sym, c_hi, lo, hi, vec), load_chunk(P.idx, c_hi, lo, hi, vec),
+                                 lo, hi, P0, perr);
+    prep_chunk<V, ALIAS, BYPASS>(P, c_hi - 1, load_chunk(P.sym, c_hi - 1, lo, hi, vec),
+                                 load_chunk(P.idx, c_hi - 1, lo, hi, vec), lo, hi, P1, perr);
+    int4 s2 = load_chunk(P.sym, c_hi - 2, lo, hi, vec), k2 = load_chunk(P.idx, c_hi - 2, lo, hi, vec);
+    int4 s3 = load_chunk(P.sym, c_hi - 3, lo, hi, vec), k3 = load_chunk(P.idx, c_hi - 3, lo, hi, vec);
+    for (int64_t c = c_hi; c >= c_lo; --c) {
+      const int4 s4 = load_chunk(P.sym, c - 4, lo, hi, vec), k4 = load_chunk(P.idx, c - 4, lo, hi, vec);
+      prep_chunk<V, ALIAS, BYPASS>(P, c - 2, s2, k2, lo, hi, P2, perr);
+      push_chain<V, ALIAS, BYPASS>(P, x, cur, P0[3]);
+      push_chain<V, ALIAS, BYPASS>(P, x, cur, P0[2]);
+      push_chain<V, ALIAS, BYPASS>(P, x, cur, P0[1]);
+      push_chain<V, ALIAS, BYPASS>(P, x, cur, P0[0]);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        P0[j] = P1[j];
+        P1[j] = P2[j];
+      }
+      s2 = s3;
+      k2 = k3;
+      s3 = s4;
+      k3 = k4;
+    }
+  }
+  store_state<V>(row, 0, x);
+  row[0] = (int32_t)((cur.p + 1) * VT<V>::WBYTES);
+  report(P.status, cur.err | perr);
+}
+
+// ---------------------------------------------------------------- four-state (i4) kernel
+// rans_cpu.cpp:89-160: the last N % 4 symbols first (state i % 4, escapes inline), then blocks
+// [i-3, i] with i = 3 (mod 4): escapes of the whole block first (symbol i-j -> state 3-j, j=0..3),
+// then the four symbols.  The four states are independent chains, so a block has 4-way ILP.
+template <int V, bool ALIAS, bool BYPASS>
+__global__ void __launch_bounds__(256) push_i4_kernel(const PushParams P) {
+  using S = typename VT<V>::State;
+  const int64_t b = my_stream(P.lanes, P.batch);
+  if (b < 0) return;
+  int32_t* row = P.stream + b * P.width;
+  PushCursor<V> cur;
+  cur.payload = reinterpret_cast<uint8_t*>(row + 1);
+  cur.p = (int64_t)row[0] / VT<V>::WBYTES - 1;
+  cur.cap = (P.width - 1) * 4 / VT<V>::WBYTES;
+  cur.err = 0;
+  S x[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) x[k] = load_state<V>(row, k);
+  uint32_t perr = 0;
+  const int32_t* sym = P.sym + b * P.nsym;
+  const int32_t* idx = P.idx + b * P.nsym;
+  const int64_t N = P.nsym;
+  const int64_t first = N % 4;
+  int64_t i = N - 1;
+  for (; i >= N - first; --i) {
+    const PushPrep r = push_prepare<V, ALIAS, BYPASS>(P, __ldg(sym + i), __ldg(idx + i), true, perr);
+    switch (i & 3) {  // state index i % 4 (i >= 0)
+      case 0: push_chain<V, ALIAS, BYPASS>(P, x[0], cur, r); break;
+      case 1: push_chain<V, ALIAS, BYPASS>(P, x[1], cur, r); break;
+      case 2: push_chain<V, ALIAS, BYPASS>(P, x[2], cur, r); break;
+      default: push_chain<V, ALIAS, BYPASS>(P, x[3], cur, r); break;
+    }
+  }
+  for (; i >= 0; i -= 4) {
+    PushPrep r[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) r[j] = push_prepare<V, ALIAS, BYPASS>(P, __ldg(sym + i - j), __ldg(idx + i - j), true, perr);
+    if constexpr (BYPASS) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (!(r[j].flags & PREP_SKIP) && (r[j].flags & PREP_ESC)) {
+          push_escape<V>(x[3 - j], cur, r[j].raw, P.bp);
+        }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) r[j].flags &= ~PREP_ESC;  // escapes already pushed
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) push_chain<V, ALIAS, BYPASS>(P, x[3 - j], cur, r[j]);
+  }
+#pragma unroll
+  for (int k = 0; k < 4; ++k) store_state<V>(row, k, x[k]);
+  row[0] = (int32_t)((cur.p + 1) * VT<V>::WBYTES);
+  report(P.status, cur.err | perr);
+}
+
+// ---------------------------------------------------------------- host side
+size_t push_workspace_bytes(int variant, int64_t ntables, int64_t enc_stride) {
+  (void)variant;
+  return align_up((size_t)ntables * sizeof(TableInfo)) + align_up((size_t)ntables * enc_stride * sizeof(uint4));
+}
+
+template <int V, bool ALIAS, bool BYPASS>
+static void launch_push(const PushParams& P, int interleave, const LaunchShape& L, cudaStream_t s) {
+  if (interleave == 4) push_i4_kernel<V, ALIAS, BYPASS><<<L.blocks, L.threads, 0, s>>>(P);
+  else push_i1_kernel<V, ALIAS, BYPASS><<<L.blocks, L.threads, 0, s>>>(P);
+}
+
+template <int V>
+static void launch_push_v(const PushParams& P, bool alias, bool bypass, int interleave, const LaunchShape& L,
+                          cudaStream_t s) {
+  if (alias) {
+    if (bypass) launch_push<V, true, true>(P, interleave, L, s);
+    else launch_push<V, true, false>(P, interleave, L, s);
+  } else {
+    if (bypass) launch_push<V, false, true>(P, interleave, L, s);
+    else launch_push<V, false, false>(P, interleave, L, s);
+  }
+}
+
+int64_t push_entry_stride(int64_t cdf_width, int fp) {
+  // entries exist for v < cdf_width - 1, and no usable table has more than 2^fp + 1 symbols
+  const int64_t a = cdf_width - 1, b = ((int64_t)1 << fp) + 1;
+  return a < b ? a : b;
+}
+
+int push_impl(int variant, int use_alias, int interleave, int32_t* stream, int64_t batch, int64_t width,
+              const int32_t* symbols, const int32_t* indexes, int64_t nsym, const int32_t* cdfs, int64_t ntables,
+              int64_t cdf_width, const int32_t* sizes, const int32_t* offsets, int fp, int bypass, int bp,
+              void* workspace, size_t ws_bytes, uint32_t* status, cudaStream_t s, bool allow_alloc) {
+  int rc = check_coding_args(variant, interleave, stream, batch, width, indexes, nsym, cdfs, ntables, cdf_width,
+                             sizes, fp, bypass, bp);
+  if (rc != TANS_OK) return rc;
+  if (nsym > 0 && !symbols) return TANS_E_INVALID_ARGUMENT;
+  if (batch == 0) return TANS_OK;
+  const int64_t stride = push_entry_stride(cdf_width, fp);
+  const size_t need = push_workspace_bytes(variant, ntables, stride);
+  void* ws = workspace;
+  bool owned = false;
+  if (!ws) {
+    if (!allow_alloc) return TANS_E_WORKSPACE;
+    if (cudaMallocAsync(&ws, need, s) != cudaSuccess) return TANS_E_CUDA;
+    owned = true;
+  } else if (ws_bytes < need) {
+    return TANS_E_WORKSPACE;
+  }
+  TableInfo* tinfo = reinterpret_cast<TableInfo*>(ws);
+  uint4* enc = reinterpret_cast<uint4*>(reinterpret_cast<char*>(ws) + align_up((size_t)ntables * sizeof(TableInfo)));
+  const int dev_sms = sm_count();
+  {
+    const int64_t n = ntables;
+    const int blocks = (int)std::min<int64_t>((n + 255) / 256, 4 * (int64_t)dev_sms);
+    build_table_info_kernel<<<blocks > 0 ? blocks : 1, 256, 0, s>>>(sizes, offsets, ntables, fp, tinfo);
+    const int64_t m = ntables * stride;
+    const int eb = (int)std::min<int64_t>((m + 255) / 256, 16 * (int64_t)dev_sms);
+    if (m > 0) {
+      if (variant == TANS_RANS64) build_push_entries_kernel<0><<<eb, 256, 0, s>>>(cdfs, ntables, cdf_width, stride, enc);
+      else if (variant == TANS_RANS32) build_push_entries_kernel<1><<<eb, 256, 0, s>>>(cdfs, ntables, cdf_width, stride, enc);
+      else build_push_entries_kernel<2><<<eb, 256, 0, s>>>(cdfs, ntables, cdf_width, stride, enc);
+    }
+  }
+  PushParams P;
+  P.stream = stream;
+  P.batch = batch;
+  P.width = width;
+  P.sym = symbols;
+  P.idx = indexes;
+  P.nsym = nsym;
+  P.enc = enc;
+  P.enc_stride = stride;
+  P.tinfo = tinfo;
+  P.ntables = ntables;
+  P.cdfs = cdfs;
+  P.cdf_width = cdf_width;
+  P.fp = fp;
+  P.bp = bp;
+  P.status = status;
+  P.vec = ((reinterpret_cast<uintptr_t>(symbols) | reinterpret_cast<uintptr_t>(indexes)) & 15u) == 0;
+  const LaunchShape L = pick_launch(batch, dev_sms);
+  P.lanes = L.lanes;
+  if (variant == TANS_RANS64) launch_push_v<0>(P, use_alias != 0, bypass != 0, interleave, L, s);
+  else if (variant == TANS_RANS32) launch_push_v<1>(P, use_alias != 0, bypass != 0, interleave, L, s);
+  else launch_push_v<2>(P, use_alias != 0, bypass != 0, interleave, L, s);
+  if (owned) cudaFreeAsync(ws, s);
+  return cudaGetLastError() == cudaSuccess ? TANS_OK : TANS_E_CUDA;
+}
+
+}  // namespace tans
+
+extern "C" size_t tans_push_workspace_size(int variant, int64_t num_tables, int64_t cdf_width) {
+  // the entry stride depends on fp only through the 2^fp + 1 cap; size for the widest case
+  return tans::push_workspace_bytes(variant, num_tables, cdf_width > 1 ? cdf_width - 1 : 0);
+}
+
+extern "C" int tans_push(int variant, int use_alias, int num_interleaves, int32_t* stream, int64_t batch,
+                         int64_t stream_width, const int32_t* symbols, const int32_t* indexes, int64_t num_symbols,
+                         const int32_t* cdfs, int64_t num_tables, int64_t cdf_width, const int32_t* cdf_sizes,
+                         const int32_t* offsets, int freq_precision, int bypass_coding, int bypass_precision,
+                         void* workspace, size_t workspace_bytes, uint32_t* dev_status, void* cuda_stream) {
+  return tans::push_impl(variant, use_alias, num_interleaves, stream, batch, stream_width, symbols, indexes,
+                         num_symbols, cdfs, num_tables, cdf_width, cdf_sizes, offsets, freq_precision, bypass_coding,
+                         bypass_precision, workspace, workspace_bytes, dev_status,
+                         reinterpret_cast<cudaStream_t>(cuda_stream), true);
+}
