@@ -105,7 +105,8 @@ def test_golden_through_c_abi(name):
     torch.cuda.synchronize()
     assert status.item() == 0
     assert np.array_equal(out.cpu().numpy(), d["decoded"])
-    assert same_rows(stream.cpu().numpy(), d["popped"])
+    got = stream.cpu().numpy()  # popped in place on the push-width row: compare lengths and payload
+    assert np.array_equal(got[:, 0], d["popped"][:, 0]) and G.payload_bytes(got) == G.payload_bytes(d["popped"])
 
 
 @pytest.mark.parametrize("variant", VARIANTS)
