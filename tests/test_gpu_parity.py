@@ -127,8 +127,8 @@ def test_streaming_pushes_and_partial_pops(C, variant):
     assert C.device_status() == 0
 
 
-def _random_case(rng, variant, bypass, K=5, A=40):
-    fp = FP[variant]
+def _random_case(rng, variant, bypass, K=5, A=40, fp=None):
+    fp = FP[variant] if fp is None else fp
     pm = rng.integers(1, 1024, (K, A)).astype(np.float32)
     pm = np.concatenate([pm, np.ones((K, 1), np.float32)], 1)
     pm /= pm.sum(1, keepdims=True)
@@ -142,13 +142,19 @@ def _random_case(rng, variant, bypass, K=5, A=40):
 @pytest.mark.parametrize("bypass", [False, True])
 @pytest.mark.parametrize("interleave", [1, 4])
 @pytest.mark.parametrize("lookup", ["search", "invcdf", "alias"])
-def test_random_against_oracle(C, variant, bypass, interleave, lookup):
-    """Seeded cases with odd lengths and misaligned rows (vector and scalar load paths)."""
+@pytest.mark.parametrize("table_path", ["fused", "direct", "fused_small"])
+def test_random_against_oracle(C, variant, bypass, interleave, lookup, table_path, monkeypatch):
+    """Seeded cases with odd lengths and misaligned rows (vector and scalar load paths), through
+    each decode table path: fused table in L2 ("fused"), fused table small enough for shared
+    memory ("fused_small", fp 11), and the caller's tables read directly ("direct")."""
+    monkeypatch.setenv("TORCH_ANS_B200_FUSED", "0" if table_path == "direct" else "1")
     if lookup == "alias" and interleave == 4:
         pytest.skip("the reference has no 4-state alias op")
     if lookup == "invcdf" and interleave == 4 and variant == "rans64":
         pytest.skip("the reference has no rans64_i4_invcdf_pop")
-    rng = np.random.default_rng(zlib.crc32(f"{variant}-{bypass}-{interleave}-{lookup}".encode()))
+    if table_path != "fused" and interleave == 4:
+        pytest.skip("4-state pops read the caller's tables directly in every mode")
+    rng = np.random.default_rng(zlib.crc32(f"{variant}-{bypass}-{interleave}-{lookup}-{table_path}".encode()))
     if lookup == "alias":
         fp = 12
         K, sp = 3, 5
@@ -161,7 +167,7 @@ def test_random_against_oracle(C, variant, bypass, interleave, lookup):
         assert ok == K
         lo, hi = (-5, A + 5) if bypass else (0, A)
     else:
-        fp, cdfs, sizes, offs = _random_case(rng, variant, bypass)
+        fp, cdfs, sizes, offs = _random_case(rng, variant, bypass, fp=11 if table_path == "fused_small" else None)
         push_c = cdfs
         pop_c = np.concatenate([cdfs, O.inverse_quantized_cdf(cdfs, fp)], 1) if lookup == "invcdf" else cdfs
         A = cdfs.shape[1] - 2

@@ -39,6 +39,7 @@ struct PushParams {
   uint32_t* status;
   int lanes;
   int vec;
+  int tin_smem;  // per-table info staged in shared memory
 };
 
 // ---------------------------------------------------------------- prep: table info + entries
@@ -214,31 +215,56 @@ __device__ __forceinline__ void push_chain(const PushParams& P, typename VT<V>::
   }
 }
 
-__device__ __forceinline__ int4 load_chunk(const int32_t* a, int64_t c, int64_t lo, int64_t hi, bool vec) {
-  const int64_t g = c * 4;
-  if (vec && g >= lo && g + 4 <= hi) return __ldg(reinterpret_cast<const int4*>(a) + c);
-  int4 r = make_int4(0, 0, 0, 0);
-  if (g >= lo && g < hi) r.x = __ldg(a + g);
-  if (g + 1 >= lo && g + 1 < hi) r.y = __ldg(a + g + 1);
-  if (g + 2 >= lo && g + 2 < hi) r.z = __ldg(a + g + 2);
-  if (g + 3 >= lo && g + 3 < hi) r.w = __ldg(a + g + 3);
-  return r;
-}
-
-template <int V, bool ALIAS, bool BYPASS>
-__device__ __forceinline__ void prep_chunk(const PushParams& P, int64_t c, int4 s4, int4 k4, int64_t lo, int64_t hi,
-                                           PushPrep (&out)[4], uint32_t& err) {
-  const int64_t g = c * 4;
-  out[0] = push_prepare<V, ALIAS, BYPASS>(P, s4.x, k4.x, g >= lo && g < hi, err);
-  out[1] = push_prepare<V, ALIAS, BYPASS>(P, s4.y, k4.y, g + 1 >= lo && g + 1 < hi, err);
-  out[2] = push_prepare<V, ALIAS, BYPASS>(P, s4.z, k4.z, g + 2 >= lo && g + 2 < hi, err);
-  out[3] = push_prepare<V, ALIAS, BYPASS>(P, s4.w, k4.w, g + 3 >= lo && g + 3 < hi, err);
-}
-
 // ---------------------------------------------------------------- single-state kernel
+// Software pipeline over chunks of 4 symbols (walked from the end of the row to its start), all
+// staging in shared memory so nothing in flight is ever held in a register:
+//   time t: (1) cp.async the symbol/index chunk x = c_hi - t                      (raw ring)
+//           (2) prep chunk x + L1: table info, escape transform, cp.async of the  (entry ring)
+//               four 16-byte encode entries
+//           (3) commit; wait until at most L2-1 groups are pending
+//           (4) run the serial chain over chunk x + L1 + L2 (its entries landed)
+// Ring slots are laid out [slot][thread] so a warp's 16-byte accesses hit distinct banks.
+constexpr int PUSH_RS = 8;  // raw slots (> L1)
+constexpr int PUSH_ES = 4;  // entry slots (> L2)
+constexpr int PUSH_L1 = 4;
+constexpr int PUSH_L2 = 3;
+constexpr int64_t kTinfoSmemMax = 4096;  // tables whose info is staged in shared memory
+
+__host__ __device__ constexpr int push_smem_per_thread(bool alias, bool bypass) {
+  return 2 * PUSH_RS * 16 + PUSH_ES * 4 * 16 + PUSH_ES * 4 + (bypass ? PUSH_ES * 16 : 0) + (alias ? PUSH_ES * 16 : 0);
+}
+
+__device__ __forceinline__ void issue_raw_chunk(int4* dst, const int32_t* a, int64_t c, int64_t total, bool vec) {
+  const int64_t g = c * 4;
+  if (vec && g >= 0 && g + 4 <= total) {
+    cp_async16(dst, a + g, 16);
+    return;
+  }
+  int32_t* d = reinterpret_cast<int32_t*>(dst);
+#pragma unroll
+  for (int e = 0; e < 4; ++e)
+    if (g + e >= 0 && g + e < total) cp_async4(d + e, a + g + e);
+}
+
 template <int V, bool ALIAS, bool BYPASS>
 __global__ void __launch_bounds__(256) push_i1_kernel(const PushParams P) {
   using S = typename VT<V>::State;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  const int T = blockDim.x, tid = threadIdx.x;
+  int4* raw_sym = reinterpret_cast<int4*>(smem_raw);
+  int4* raw_idx = raw_sym + PUSH_RS * T;
+  uint4* ent = reinterpret_cast<uint4*>(raw_idx + PUSH_RS * T);
+  uint32_t* flg = reinterpret_cast<uint32_t*>(ent + PUSH_ES * 4 * T);
+  int4* escv = reinterpret_cast<int4*>(flg + PUSH_ES * T);
+  int4* kslot = escv + (BYPASS ? PUSH_ES * T : 0);
+  TableInfo* tsm = reinterpret_cast<TableInfo*>(kslot + (ALIAS ? PUSH_ES * T : 0));
+  const bool tin_smem = P.tin_smem != 0;
+  if (tin_smem) {
+    for (int64_t k = tid; k < P.ntables; k += T) tsm[k] = P.tinfo[k];
+    __syncthreads();
+  }
+  const TableInfo* tin = tin_smem ? tsm : P.tinfo;
+
   const int64_t b = my_stream(P.lanes, P.batch);
   if (b < 0) return;
   int32_t* row = P.stream + b * P.width;
@@ -249,35 +275,99 @@ __global__ void __launch_bounds__(256) push_i1_kernel(const PushParams P) {
   cur.err = 0;
   S x = load_state<V>(row, 0);
   uint32_t perr = 0;
+  const int64_t lo = b * P.nsym, hi = lo + P.nsym, total = P.batch * P.nsym;
+  const bool vec = P.vec != 0;
 
-  const int64_t lo = b * P.nsym, hi = lo + P.nsym;
   if (P.nsym > 0) {
     const int64_t c_hi = (hi - 1) >> 2, c_lo = lo >> 2;
-    const bool vec = P.vec != 0;
-    PushPrep P0[4], P1[4], P2[4];
-    prep_chunk<V, ALIAS, BYPASS>(P, c_hi, load_chunk(P.sym, c_hi, lo, hi, vec), load_chunk(P.idx, c_hi, lo, hi, vec),
-                                 lo, hi, P0, perr);
-    prep_chunk<V, ALIAS, BYPASS>(P, c_hi - 1, load_chunk(P.sym, c_hi - 1, lo, hi, vec),
-                                 load_chunk(P.idx, c_hi - 1, lo, hi, vec), lo, hi, P1, perr);
-    int4 s2 = load_chunk(P.sym, c_hi - 2, lo, hi, vec), k2 = load_chunk(P.idx, c_hi - 2, lo, hi, vec);
-    int4 s3 = load_chunk(P.sym, c_hi - 3, lo, hi, vec), k3 = load_chunk(P.idx, c_hi - 3, lo, hi, vec);
-    for (int64_t c = c_hi; c >= c_lo; --c) {
-      const int4 s4 = load_chunk(P.sym, c - 4, lo, hi, vec), k4 = load_chunk(P.idx, c - 4, lo, hi, vec);
-      prep_chunk<V, ALIAS, BYPASS>(P, c - 2, s2, k2, lo, hi, P2, perr);
-      push_chain<V, ALIAS, BYPASS>(P, x, cur, P0[3]);
-      push_chain<V, ALIAS, BYPASS>(P, x, cur, P0[2]);
-      push_chain<V, ALIAS, BYPASS>(P, x, cur, P0[1]);
-      push_chain<V, ALIAS, BYPASS>(P, x, cur, P0[0]);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        P0[j] = P1[j];
-        P1[j] = P2[j];
+    const int64_t t_end = (c_hi - c_lo) + PUSH_L1 + PUSH_L2;
+    for (int64_t t = 0; t <= t_end; ++t) {
+      // (1) raw chunk
+      const int64_t xr = c_hi - t;
+      if (xr >= c_lo) {
+        const int rs = (int)(xr & (PUSH_RS - 1));
+        issue_raw_chunk(raw_sym + rs * T + tid, P.sym, xr, total, vec);
+        issue_raw_chunk(raw_idx + rs * T + tid, P.idx, xr, total, vec);
       }
-      s2 = s3;
-      k2 = k3;
-      s3 = s4;
-      k3 = k4;
+      // (2) prep
+      const int64_t xp = xr + PUSH_L1;
+      if (xp >= c_lo && xp <= c_hi) {
+        const int rs = (int)(xp & (PUSH_RS - 1)), es = (int)(xp & (PUSH_ES - 1));
+        const int4 s4 = raw_sym[rs * T + tid], k4 = raw_idx[rs * T + tid];
+        const int32_t sv[4] = {s4.x, s4.y, s4.z, s4.w}, kv[4] = {k4.x, k4.y, k4.z, k4.w};
+        uint32_t flags = 0;
+        int32_t esc[4] = {0, 0, 0, 0};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int64_t g = xp * 4 + j;
+          uint32_t f = PREP_SKIP;
+          if (g >= lo && g < hi) {
+            const int32_t k = kv[j];
+            if (k < 0 || (int64_t)k >= P.ntables) {
+              perr |= DEV_BAD_INDEX;
+            } else {
+              const TableInfo ti = tin_smem ? tin[k] : load_tinfo(P.tinfo, k);
+              int32_t v = (int32_t)((uint32_t)sv[j] - (uint32_t)ti.offset);
+              const int32_t maxv = ti.size - 2;
+              f = 0;
+              if constexpr (BYPASS) {
+                if (v < 0) {
+                  esc[j] = -2 * v - 1;
+                  v = maxv;
+                } else if (v >= maxv) {
+                  esc[j] = 2 * (v - maxv);
+                  v = maxv;
+                }
+                if (v == maxv) f = PREP_ESC;
+              }
+              if (v < 0 || v >= ti.size - 1 || (int64_t)v >= P.enc_stride) {
+                perr |= DEV_BAD_VALUE;
+                f = PREP_SKIP;
+              } else {
+                cp_async16(ent + (es * 4 + j) * T + tid, P.enc + (int64_t)k * P.enc_stride + v, 16);
+              }
+            }
+          }
+          flags |= f << (8 * j);
+        }
+        flg[es * T + tid] = flags;
+        if constexpr (BYPASS) escv[es * T + tid] = make_int4(esc[0], esc[1], esc[2], esc[3]);
+        if constexpr (ALIAS) kslot[es * T + tid] = k4;
+      }
+      // (3)
+      cp_async_commit();
+      cp_async_wait<PUSH_L2 - 1>();
+      // (4) chain, last symbol of the chunk first
+      const int64_t xc = xp + PUSH_L2;
+      if (xc >= c_lo && xc <= c_hi) {
+        const int es = (int)(xc & (PUSH_ES - 1));
+        const uint32_t flags = flg[es * T + tid];
+        int4 escq = make_int4(0, 0, 0, 0), kq = make_int4(0, 0, 0, 0);
+        if constexpr (BYPASS) escq = escv[es * T + tid];
+        if constexpr (ALIAS) kq = kslot[es * T + tid];
+        const int32_t escs[4] = {escq.x, escq.y, escq.z, escq.w};
+        const int32_t ks[4] = {kq.x, kq.y, kq.z, kq.w};
+#pragma unroll
+        for (int j = 3; j >= 0; --j) {
+          const uint32_t f = (flags >> (8 * j)) & 0xffu;
+          if (f & PREP_SKIP) continue;
+          PushPrep r;
+          r.flags = f;
+          r.raw = escs[j];
+          r.e = ent[(es * 4 + j) * T + tid];
+          r.rbase = 0;
+          r.rcap = 0;
+          if constexpr (ALIAS) {
+            const TableInfo ti = tin_smem ? tin[ks[j]] : load_tinfo(P.tinfo, ks[j]);
+            r.rbase = (int64_t)ks[j] * P.cdf_width + ti.size;
+            const int64_t cap = P.cdf_width - ti.size;
+            r.rcap = cap <= 0 ? 0 : (cap > 0x7fffffff ? 0x7fffffff : (int32_t)cap);
+          }
+          push_chain<V, ALIAS, BYPASS>(P, x, cur, r);
+        }
+      }
     }
+    cp_async_wait<0>();
   }
   store_state<V>(row, 0, x);
   row[0] = (int32_t)((cur.p + 1) * VT<V>::WBYTES);
@@ -347,8 +437,15 @@ size_t push_workspace_bytes(int variant, int64_t ntables, int64_t enc_stride) {
 
 template <int V, bool ALIAS, bool BYPASS>
 static void launch_push(const PushParams& P, int interleave, const LaunchShape& L, cudaStream_t s) {
-  if (interleave == 4) push_i4_kernel<V, ALIAS, BYPASS><<<L.blocks, L.threads, 0, s>>>(P);
-  else push_i1_kernel<V, ALIAS, BYPASS><<<L.blocks, L.threads, 0, s>>>(P);
+  if (interleave == 4) {
+    push_i4_kernel<V, ALIAS, BYPASS><<<L.blocks, L.threads, 0, s>>>(P);
+    return;
+  }
+  size_t smem = (size_t)L.threads * push_smem_per_thread(ALIAS, BYPASS);
+  if (P.tin_smem) smem += (size_t)P.ntables * sizeof(TableInfo);
+  if (smem > 48 * 1024)
+    cudaFuncSetAttribute(push_i1_kernel<V, ALIAS, BYPASS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  push_i1_kernel<V, ALIAS, BYPASS><<<L.blocks, L.threads, smem, s>>>(P);
 }
 
 template <int V>
@@ -423,6 +520,11 @@ int push_impl(int variant, int use_alias, int interleave, int32_t* stream, int64
   P.vec = ((reinterpret_cast<uintptr_t>(symbols) | reinterpret_cast<uintptr_t>(indexes)) & 15u) == 0;
   const LaunchShape L = pick_launch(batch, dev_sms);
   P.lanes = L.lanes;
+  P.tin_smem = (ntables <= kTinfoSmemMax &&
+                (size_t)L.threads * push_smem_per_thread(use_alias != 0, bypass != 0) + (size_t)ntables * sizeof(TableInfo) <=
+                    200 * 1024)
+                   ? 1
+                   : 0;
   if (variant == TANS_RANS64) launch_push_v<0>(P, use_alias != 0, bypass != 0, interleave, L, s);
   else if (variant == TANS_RANS32) launch_push_v<1>(P, use_alias != 0, bypass != 0, interleave, L, s);
   else launch_push_v<2>(P, use_alias != 0, bypass != 0, interleave, L, s);
