@@ -260,7 +260,17 @@ def test_device_stream_helpers():
     from torch_ans_b200 import _C
     for nb in (1, 2, 4, 8):
         for ns in (None, len(segs)):
+            if nb == 1 and max(len(x) for x in segs) > 255:
+                # the reference's struct.pack("B", n) raises for n > 255; so does the device path
+                with pytest.raises(ValueError):
+                    _C.stream_to_merged_bytes(st, nb, ns)
+                continue
             assert _C.stream_to_merged_bytes(st, nb, ns) == O.merge_bytes(segs, nb, ns)
+            packed = _C.stream_to_merged_tensor(st, nb, ns)
+            assert bytes(packed.cpu().numpy().tobytes()) == O.merge_bytes(segs, nb, ns)
+            if nb != 8:
+                back = _C.merged_tensor_to_stream(packed.cpu(), nb, ns, "cuda")
+                assert same_rows(back.cpu().numpy(), O.byte_strings_to_stream(segs))
     # scatter back
     lens = torch.tensor([len(x) for x in segs], dtype=torch.int32, device="cuda")
     offs = torch.tensor(np.concatenate([[0], np.cumsum([len(x) for x in segs])[:-1]]), dtype=torch.int64, device="cuda")
@@ -269,3 +279,63 @@ def test_device_stream_helpers():
     assert lib.tans_scatter_payloads(flat.data_ptr(), offs.data_ptr(), lens.data_ptr(), out.data_ptr(), st.shape[0],
                                      st.shape[1], cs) == 0
     assert same_rows(out.cpu().numpy(), d["pushed"])
+
+
+LAYOUTS = ["fused_smem", "split_smem", "cdf_smem", "fused_global", "split_global", "generic"]
+
+
+@pytest.mark.parametrize("layout", LAYOUTS)
+@pytest.mark.parametrize("variant", VARIANTS)
+@pytest.mark.parametrize("lookup", ["search", "invcdf", "alias"])
+@pytest.mark.parametrize("bypass", [False, True])
+@pytest.mark.parametrize("spt", ["1", "4"])
+def test_fast_pop_layouts(C, layout, variant, lookup, bypass, spt, monkeypatch):
+    """Aligned rows with a length divisible by 4 take the fast pop kernel; every table layout it
+    can use is forced in turn (an infeasible one falls back to the automatic choice) and must
+    decode exactly what the oracle decodes, with the same final stream rows."""
+    if layout in ("split_smem", "cdf_smem", "split_global") and lookup == "alias":
+        pytest.skip("alias offsets depend on cum: fused layouts only")
+    if layout == "cdf_smem" and lookup != "search":
+        pytest.skip("shared-memory bisection is the search lookup")
+    if layout == "fused_global" and lookup != "alias" and spt == "4":
+        pytest.skip("fused_global serves alias tables")
+    monkeypatch.setenv("TORCH_ANS_B200_POP_LAYOUT", layout)
+    monkeypatch.setenv("TORCH_ANS_B200_SPT", spt)
+    rng = np.random.default_rng(zlib.crc32(f"fast-{layout}-{variant}-{lookup}-{bypass}-{spt}".encode()))
+    if lookup == "alias":
+        fp, K, sp = 12, 3, 5
+        A = 1 << sp
+        pm = rng.random((K, A)) + 0.05
+        cdfs = O.pmf_to_quantized_cdf((pm / pm.sum(1, keepdims=True)).astype(np.float32), fp)
+        sizes = np.full(K, A + 1, np.int32)
+        offs = rng.integers(-3, 3, K).astype(np.int32)
+        push_c, pop_c, ok = O.alias_build_table(cdfs, sizes, sp, fp)
+        lo, hi = (-5, A + 5) if bypass else (0, A)
+    else:
+        fp = 11 if layout.endswith("smem") else FP[variant]
+        fp, cdfs, sizes, offs = _random_case(rng, variant, bypass, K=4, A=30, fp=fp)
+        push_c = cdfs
+        pop_c = np.concatenate([cdfs, O.inverse_quantized_cdf(cdfs, fp)], 1) if lookup == "invcdf" else cdfs
+        A = cdfs.shape[1] - 2
+        lo, hi = (-20, A + 20) if bypass else (0, A + 1)
+    K = cdfs.shape[0]
+    B, N = 45, 1000
+    idx = rng.integers(0, K, (B, N)).astype(np.int32)
+    sym = rng.integers(lo, hi, (B, N)).astype(np.int32)
+    if not bypass:
+        sym = (np.clip(sym, 0, sizes[idx] - 2) + offs[idx]).astype(np.int32)
+    ref, perr = O.push(variant, O.init_stream(variant, B), sym, idx, push_c, sizes, offs, fp, bypass, 4,
+                       alias=lookup == "alias")
+    assert perr == 0
+    ref_pop = ref.copy()
+    dec_ref, derr = O.pop(variant, ref_pop, idx, pop_c, sizes, offs, fp, bypass, 4, lookup=lookup)
+    assert derr == 0 and np.array_equal(dec_ref, sym)
+    push, pop = op_names(variant, 1, lookup == "alias", lookup)
+    kw = dict(freq_precision=fp, bypass_coding=bypass, bypass_precision=4)
+    st = getattr(C, f"{variant}_init_stream")(B).cuda()
+    getattr(C, push)(st, t(sym), t(idx), t(push_c), t(sizes), t(offs), **kw)
+    assert same_rows(st.cpu().numpy(), ref)
+    dec = getattr(C, pop)(st, t(idx), t(pop_c), t(sizes), t(offs), **kw)
+    assert C.device_status() == 0
+    assert np.array_equal(dec.cpu().numpy(), sym)
+    assert same_rows(st.cpu().numpy(), ref_pop)

@@ -287,6 +287,10 @@ py::bytes stream_to_merged_bytes(const Tensor& stream, int64_t num_bytes_length,
   const int64_t* l = lens.data_ptr<int64_t>();
   int64_t* o = offs.data_ptr<int64_t>();
   for (int64_t b = 0; b < B; ++b) {
+    // struct.pack of the reference's length format rejects lengths that do not fit
+    if (b < prefix_rows && prefix_bytes < 4 && l[b] >= ((int64_t)1 << (8 * prefix_bytes)))
+      throw py::value_error("segment length " + std::to_string(l[b]) + " does not fit in a " +
+                            std::to_string(prefix_bytes) + "-byte length prefix");
     o[b] = total;
     total += (b < prefix_rows ? prefix_bytes : 0) + (l[b] > 0 ? l[b] : 0);
   }
@@ -313,6 +317,12 @@ Tensor stream_to_merged_tensor(const Tensor& stream, int64_t num_bytes_length, s
   if (num_segments.has_value()) TORCH_CHECK(B <= *num_segments, "Number of segments exceed predefined ", *num_segments);
   const int64_t prefix_rows = num_segments.has_value() ? std::min<int64_t>(B, *num_segments - 1) : B;
   Tensor lens = s.select(1, 0).to(torch::kInt64).clamp(0, (s.size(1) - 1) * 4);
+  if (prefix_bytes < 4 && prefix_rows > 0) {
+    const int64_t longest = lens.narrow(0, 0, prefix_rows).max().item<int64_t>();
+    if (longest >= ((int64_t)1 << (8 * prefix_bytes)))
+      throw py::value_error("segment length " + std::to_string(longest) + " does not fit in a " +
+                            std::to_string(prefix_bytes) + "-byte length prefix");
+  }
   Tensor rec = lens + (torch::arange(B, lens.options()) < prefix_rows).to(torch::kInt64) * prefix_bytes;
   Tensor ends = torch::cumsum(rec, 0);
   Tensor offs = ends - rec;

@@ -12,170 +12,19 @@
 
 #include <algorithm>
 #include <cstdlib>
+#include <string>
 
 #include "../../include/torch_ans_b200.h"
 #include "launch.cuh"
 #include "rans_device.cuh"
 #include "rans_host.h"
+#include "rans_pop.cuh"
+#include "rans_pop_fast.cuh"
 
 namespace tans {
 
 __global__ void build_table_info_kernel(const int32_t* sizes, const int32_t* offsets, int64_t ntables, int fp,
                                         TableInfo* out);
-
-struct PopParams {
-  int32_t* stream;
-  int64_t batch, width;
-  int32_t* out;
-  const int32_t* idx;
-  int64_t nsym;
-  const int32_t* cdfs;
-  int64_t ntables, cdf_width;
-  const TableInfo* tinfo;
-  int fp, bp;
-  uint32_t* status;
-  int lanes;
-  int vec;
-  const uint32_t* fD;  // fused decode table (nullptr: direct lookups)
-  const uint16_t* fS;
-  int fused_smem;      // fused table staged in shared memory
-  int tin_smem;        // per-table info staged in shared memory
-  int vec_out;         // out is 16-byte aligned
-};
-
-template <int V> struct PopCursor {
-  const uint8_t* payload;  // row + 1
-  int64_t p;               // index of the next word to read
-  int64_t first;           // first word index after the state slots
-  int64_t cap;             // words in the row (reads at or above are refused)
-  uint32_t err;
-
-  __device__ __forceinline__ void refill(typename VT<V>::State& x) {
-    using S = typename VT<V>::State;
-    using W = typename VT<V>::Word;
-#pragma unroll
-    for (int t = 0; t < VT<V>::MAX_RENORM; ++t) {
-      if ((unsigned long long)x < VT<V>::LB) {
-        S w = 0;
-        if (p >= first && p < cap) w = (S)__ldg(reinterpret_cast<const W*>(payload) + p);
-        else err |= DEV_UNDERFLOW;
-        x = (S)((x << VT<V>::WB) | w);
-        p -= 1;
-      }
-    }
-  }
-};
-
-// rans_pop_raw_value_step, rans_utils.hpp:327-375 (escape value, rare path)
-template <int V>
-__device__ __noinline__ int32_t pop_escape(typename VT<V>::State& x, PopCursor<V>& c, int bp) {
-  using S = typename VT<V>::State;
-  const int32_t maxb = (int32_t)((1u << bp) - 1u);
-  int32_t val = (int32_t)(x & (S)maxb);
-  x >>= bp;
-  c.refill(x);
-  int32_t n = val;
-  while (val == maxb && n <= 32) {
-    val = (int32_t)(x & (S)maxb);
-    x >>= bp;
-    c.refill(x);
-    n += val;
-  }
-  if (n > 32) {
-    c.err |= DEV_BAD_ESCAPE;
-    n = 0;
-  }
-  uint32_t raw = 0;
-  for (int32_t j = 0; j < n; ++j) {
-    val = (int32_t)(x & (S)maxb);
-    x >>= bp;
-    c.refill(x);
-    if (j * bp < 32) raw |= (uint32_t)val << (j * bp);
-  }
-  return (int32_t)raw;
-}
-
-enum : int { LK_SEARCH = 0, LK_INVCDF = 1, LK_ALIAS = 2 };
-
-// Symbol lookup of rans_utils.hpp:401-449 for one cum value of table row `row`: sets s and the
-// offset cum - start (alias: cum - alias_start) and the symbol's frequency.  Returns false where
-// the reference would index outside the row (then nothing is read out of bounds).
-template <int V, int LK>
-__device__ __forceinline__ bool lookup_symbol(const int32_t* row, const TableInfo& t, int32_t cum, int64_t cdf_width,
-                                              int fp, int64_t& s, int32_t& cum_off, int32_t& freq) {
-  using S = typename VT<V>::State;
-  const int32_t size = t.size;
-  if (size < 2 || (int64_t)size > cdf_width) return false;
-  cum_off = cum;
-  if constexpr (LK == LK_ALIAS) {
-    if (t.cut <= 0) return false;
-    const int32_t id = t.cut_log2 >= 0 ? (cum >> t.cut_log2) : (cum / t.cut);
-    const int64_t at = (int64_t)size + 4 * (int64_t)id;
-    if (at + 3 >= cdf_width) return false;
-    const int32_t cut_cdf = __ldg(row + at);
-    const int32_t other = __ldg(row + at + 1);
-    const int32_t self_off = __ldg(row + at + 2);
-    const int32_t other_off = __ldg(row + at + 3);
-    const bool hi = cum >= cut_cdf;
-    s = hi ? other : id;
-    cum_off -= hi ? other_off : self_off;
-  } else if constexpr (LK == LK_INVCDF) {
-    if ((int64_t)size + cum >= cdf_width) return false;
-    s = __ldg(row + size + cum);
-  } else {
-    // probe (cdf_size * cum) >> fp, then bisection on [0, cdf_size - 1] (rans_utils.hpp:427-448)
-    S ix = to_state<S>((int32_t)((uint32_t)size * (uint32_t)cum) >> fp);
-    uint32_t low = 0, high = (uint32_t)(size - 1);
-    while (high > low) {
-      if ((unsigned long long)ix >= (unsigned long long)size) return false;
-      if (cum >= __ldg(row + ix)) low = (uint32_t)ix + 1u;
-      else high = (uint32_t)ix;
-      ix = (S)((low + high) / 2u);
-    }
-    s = (int64_t)(unsigned long long)(S)(ix - 1);
-  }
-  if (s < 0 || s >= (int64_t)size - 1) return false;
-  const int32_t lo_c = __ldg(row + s), hi_c = __ldg(row + s + 1);
-  if constexpr (LK != LK_ALIAS) cum_off -= lo_c;
-  freq = (int32_t)((uint32_t)hi_c - (uint32_t)lo_c);
-  return true;
-}
-
-// the rest of a pop step once the lookup is done: x = D(x), refill, escape (rans_utils.hpp:473-531)
-template <int V, bool BYPASS>
-__device__ __forceinline__ int32_t pop_finish(const PopParams& P, typename VT<V>::State& x, PopCursor<V>& c,
-                                              int32_t s, int32_t cum_off, int32_t freq, int32_t maxv) {
-  using S = typename VT<V>::State;
-  x = (S)((x >> P.fp) * to_state<S>(freq) + to_state<S>(cum_off));
-  c.refill(x);
-  int32_t value = s;
-  if constexpr (BYPASS) {
-    if (value == maxv) {
-      const int32_t raw = pop_escape<V>(x, c, P.bp);
-      value = raw >> 1;
-      value = (raw & 1) ? (-value - 1) : (value + maxv);
-    }
-  }
-  return value;
-}
-
-// one symbol straight from the caller's tables.  `ok` is cleared when the step was skipped.
-template <int V, int LK, bool BYPASS>
-__device__ __forceinline__ int32_t pop_chain(const PopParams& P, typename VT<V>::State& x, PopCursor<V>& c,
-                                             int32_t k, const TableInfo& t, bool& ok) {
-  using S = typename VT<V>::State;
-  ok = false;
-  const int32_t* row = P.cdfs + (int64_t)k * P.cdf_width;
-  const int32_t cum = (int32_t)(uint32_t)(x & (S)((1ull << P.fp) - 1ull));
-  int64_t s;
-  int32_t cum_off, freq;
-  if (!lookup_symbol<V, LK>(row, t, cum, P.cdf_width, P.fp, s, cum_off, freq)) {
-    c.err |= DEV_BAD_VALUE;
-    return 0;
-  }
-  ok = true;
-  return pop_finish<V, BYPASS>(P, x, c, (int32_t)s, cum_off, freq, t.size - 2);
-}
 
 // Fused decode table: for every (table k, cum < 2^fp) the lookup above replayed once per call,
 // packed as D = (freq - 1) | (cum_off << 16) and S = s; S = 0xFFFF marks entries that do not pack
@@ -203,25 +52,41 @@ __global__ void build_fused_kernel(const int32_t* cdfs, int64_t ntables, int64_t
   }
 }
 
-__device__ __forceinline__ int4 load_idx_chunk(const int32_t* a, int64_t c, int64_t lo, int64_t hi, bool vec) {
-  const int64_t g = c * 4;
-  if (vec && g >= lo && g + 4 <= hi) return __ldg(reinterpret_cast<const int4*>(a) + c);
-  int4 r = make_int4(0, 0, 0, 0);
-  if (g >= lo && g < hi) r.x = __ldg(a + g);
-  if (g + 1 >= lo && g + 1 < hi) r.y = __ldg(a + g + 1);
-  if (g + 2 >= lo && g + 2 < hi) r.z = __ldg(a + g + 2);
-  if (g + 3 >= lo && g + 3 < hi) r.w = __ldg(a + g + 3);
-  return r;
+// Split decode tables (inverse-cdf and bisection lookups, whose offset is cum - cdf[s]):
+// S[k][cum] = s from the reference's lookup, ST[k][s] = (freq - 1) | start << 16.  S = 0xFFFF where
+// the lookup fails or s, freq or start do not pack; those steps take the direct lookup.
+template <int V, int LK>
+__global__ void build_split_s_kernel(const int32_t* cdfs, int64_t ntables, int64_t cdf_width, const TableInfo* tinfo,
+                                     int fp, int64_t st_stride, uint16_t* Sx) {
+  const int64_t M = (int64_t)1 << fp, total = ntables * M;
+  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t k = e >> fp;
+    const int32_t cum = (int32_t)(e & (M - 1));
+    const TableInfo t = tinfo[k];
+    int64_t s;
+    int32_t cum_off, freq;
+    uint16_t sv = 0xFFFFu;
+    if (lookup_symbol<V, LK>(cdfs + k * cdf_width, t, cum, cdf_width, fp, s, cum_off, freq)) {
+      const int64_t start = (int64_t)cum - cum_off;
+      if (s < st_stride && s < 0xFFFF && freq >= 1 && freq <= 65536 && start >= 0 && start <= 65535) sv = (uint16_t)s;
+    }
+    Sx[e] = sv;
+  }
 }
 
-__device__ __forceinline__ TableInfo tinfo_or_zero(const PopParams& P, int32_t k, bool in_row) {
-  if (in_row && k >= 0 && (int64_t)k < P.ntables) return load_tinfo(P.tinfo, k);
-  TableInfo t;
-  t.size = 0;
-  t.offset = 0;
-  t.cut = 0;
-  t.cut_log2 = -1;
-  return t;
+__global__ void build_split_st_kernel(const int32_t* cdfs, int64_t ntables, int64_t cdf_width, int64_t st_stride,
+                                      uint32_t* ST) {
+  const int64_t total = ntables * st_stride;
+  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t k = e / st_stride, sidx = e - k * st_stride;
+    uint32_t v = 0;
+    if (sidx + 1 < cdf_width) {
+      const int32_t start = cdfs[k * cdf_width + sidx];
+      const int32_t freq = (int32_t)((uint32_t)cdfs[k * cdf_width + sidx + 1] - (uint32_t)start);
+      v = ((uint32_t)(freq - 1) & 0xFFFFu) | ((uint32_t)start << 16);
+    }
+    ST[e] = v;
+  }
 }
 
 template <int V, int LK, bool BYPASS>
@@ -427,23 +292,39 @@ __global__ void __launch_bounds__(256) pop_i4_kernel(const PopParams P) {
 }
 
 // ---------------------------------------------------------------- host side
-constexpr int64_t kFusedMaxBytes = 128ll << 20;  // fused decode tables up to this size
+constexpr int64_t kFusedMaxBytes = 128ll << 20;  // fused tables in global memory up to this size
+constexpr int64_t kSplitMaxBytes = 256ll << 20;  // split tables in global memory up to this size
 constexpr int64_t kSmemBudget = 200 * 1024;
 
-static bool fused_enabled(int64_t ntables, int fp) {
+static int64_t split_stride(int lookup, int64_t cdf_width, int fp) {
+  // entries per table in ST: the cdf part of a row (an inverse-cdf row is [cdf | 2^fp inverse])
+  int64_t w = lookup == TANS_LOOKUP_INVCDF ? cdf_width - ((int64_t)1 << fp) : cdf_width;
+  if (w < 2) w = 2;
+  const int64_t cap = ((int64_t)1 << fp) + 1;
+  return std::min(w - 1, cap);
+}
+
+static int64_t fused_bytes(int64_t ntables, int fp) { return ntables * ((int64_t)6 << fp); }
+static int64_t split_bytes(int lookup, int64_t ntables, int64_t cdf_width, int fp) {
+  return ntables * ((int64_t)2 << fp) + ntables * split_stride(lookup, cdf_width, fp) * 4;
+}
+
+static bool tables_enabled() {
   const char* e = std::getenv("TORCH_ANS_B200_FUSED");
-  if (e && e[0] == '0') return false;
-  return fp <= 16 && ntables * ((int64_t)6 << fp) <= kFusedMaxBytes;
+  return !(e && e[0] == '0');
 }
 
 size_t pop_workspace_bytes(int variant, int lookup, int64_t ntables, int64_t cdf_width, int fp) {
   (void)variant;
-  (void)lookup;
-  (void)cdf_width;
   size_t n = align_up((size_t)ntables * sizeof(TableInfo));
-  if (fused_enabled(ntables, fp)) {
-    const size_t m = (size_t)ntables << fp;
-    n += align_up(m * 4) + align_up(m * 2);
+  if (fp <= 16 && tables_enabled()) {
+    size_t extra = 0;
+    if (fused_bytes(ntables, fp) <= kFusedMaxBytes)
+      extra = align_up((size_t)(ntables << fp) * 4) + align_up((size_t)(ntables << fp) * 2);
+    if (lookup != TANS_LOOKUP_ALIAS && split_bytes(lookup, ntables, cdf_width, fp) <= kSplitMaxBytes)
+      extra = std::max(extra, align_up((size_t)(ntables << fp) * 2) +
+                                  align_up((size_t)ntables * split_stride(lookup, cdf_width, fp) * 4));
+    n += extra;
   }
   return n;
 }
@@ -487,15 +368,63 @@ static void launch_pop_v(const PopParams& P, int lookup, bool bypass, int interl
 }
 
 template <int V>
-static void launch_fused_build(const PopParams& P, int lookup, uint32_t* D, uint16_t* Sx, int sms, cudaStream_t s) {
+static void build_tables(const PopParams& P, int lookup, bool fused, uint32_t* D, uint16_t* Sx, uint32_t* ST,
+                         int sms, cudaStream_t s) {
   const int64_t m = P.ntables << P.fp;
-  const int blocks = (int)std::min<int64_t>((m + 255) / 256, 8 * (int64_t)sms);
-  if (lookup == TANS_LOOKUP_ALIAS)
-    build_fused_kernel<V, LK_ALIAS><<<blocks, 256, 0, s>>>(P.cdfs, P.ntables, P.cdf_width, P.tinfo, P.fp, D, Sx);
-  else if (lookup == TANS_LOOKUP_INVCDF)
-    build_fused_kernel<V, LK_INVCDF><<<blocks, 256, 0, s>>>(P.cdfs, P.ntables, P.cdf_width, P.tinfo, P.fp, D, Sx);
+  const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>((m + 255) / 256, 8 * (int64_t)sms));
+  if (fused) {
+    if (lookup == TANS_LOOKUP_ALIAS)
+      build_fused_kernel<V, LK_ALIAS><<<blocks, 256, 0, s>>>(P.cdfs, P.ntables, P.cdf_width, P.tinfo, P.fp, D, Sx);
+    else if (lookup == TANS_LOOKUP_INVCDF)
+      build_fused_kernel<V, LK_INVCDF><<<blocks, 256, 0, s>>>(P.cdfs, P.ntables, P.cdf_width, P.tinfo, P.fp, D, Sx);
+    else
+      build_fused_kernel<V, LK_SEARCH><<<blocks, 256, 0, s>>>(P.cdfs, P.ntables, P.cdf_width, P.tinfo, P.fp, D, Sx);
+    return;
+  }
+  if (lookup == TANS_LOOKUP_INVCDF)
+    build_split_s_kernel<V, LK_INVCDF><<<blocks, 256, 0, s>>>(P.cdfs, P.ntables, P.cdf_width, P.tinfo, P.fp,
+                                                              P.st_stride, Sx);
   else
-    build_fused_kernel<V, LK_SEARCH><<<blocks, 256, 0, s>>>(P.cdfs, P.ntables, P.cdf_width, P.tinfo, P.fp, D, Sx);
+    build_split_s_kernel<V, LK_SEARCH><<<blocks, 256, 0, s>>>(P.cdfs, P.ntables, P.cdf_width, P.tinfo, P.fp,
+                                                              P.st_stride, Sx);
+  const int64_t n = P.ntables * P.st_stride;
+  const int b2 = (int)std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, 8 * (int64_t)sms));
+  build_split_st_kernel<<<b2, 256, 0, s>>>(P.cdfs, P.ntables, P.cdf_width, P.st_stride, ST);
+}
+
+// launch shape of the fast kernel: streams spread over all SMs, up to 4 warps per SM, then up to
+// 4 streams per thread, then more lanes
+static LaunchShape fast_shape(int64_t streams, int sms, int& spt) {
+  LaunchShape L{1, 32, 1};
+  const int64_t per_sm = (streams + sms - 1) / sms;
+  int64_t warps = std::min<int64_t>(4, per_sm);
+  int64_t sp = (per_sm + warps - 1) / warps;
+  sp = sp >= 4 ? 4 : (sp >= 2 ? 2 : 1);
+  const int spt_env = env_int("TORCH_ANS_B200_SPT", 0);
+  if (spt_env == 1 || spt_env == 2 || spt_env == 4) sp = spt_env;
+  int64_t lanes = (per_sm + warps * sp - 1) / (warps * sp);
+  if (lanes > 32) {
+    lanes = 32;
+    warps = std::min<int64_t>(4, (per_sm + 32 * sp - 1) / (32 * sp));
+  }
+  spt = (int)sp;
+  L.lanes = (int)lanes;
+  L.threads = (int)(warps * 32);
+  L.blocks = (int)((streams + warps * lanes * sp - 1) / (warps * lanes * sp));
+  return L;
+}
+
+static int layout_override() {
+  const char* e = std::getenv("TORCH_ANS_B200_POP_LAYOUT");
+  if (!e || !*e) return -1;
+  const std::string v(e);
+  if (v == "fused_smem") return TM_FUSED_SMEM;
+  if (v == "fused_global") return TM_FUSED_GLOBAL;
+  if (v == "split_smem") return TM_SPLIT_SMEM;
+  if (v == "split_global") return TM_SPLIT_GLOBAL;
+  if (v == "cdf_smem") return TM_CDF_SMEM;
+  if (v == "generic") return 100;
+  return -1;
 }
 
 int pop_impl(int variant, int lookup, int interleave, int32_t* stream, int64_t batch, int64_t width, int32_t* out,
@@ -508,9 +437,56 @@ int pop_impl(int variant, int lookup, int interleave, int32_t* stream, int64_t b
   if (lookup < 0 || lookup > 2) return TANS_E_INVALID_ARGUMENT;
   if (nsym > 0 && !out) return TANS_E_INVALID_ARGUMENT;
   if (batch == 0) return TANS_OK;
-  const bool fused = interleave == 1 && nsym > 0 && fused_enabled(ntables, fp);
+  const int dev_sms = sm_count();
+  const bool vec_idx = (reinterpret_cast<uintptr_t>(indexes) & 15u) == 0;
+  const bool vec_out = (reinterpret_cast<uintptr_t>(out) & 15u) == 0;
+  const bool use_tables = interleave == 1 && nsym > 0 && fp <= 16 && tables_enabled();
+  const int64_t sstride = split_stride(lookup, cdf_width, fp);
+
+  // ---- plan: fast kernel + table layout, or the generic kernel
+  int tm = -1, spt = 1;
+  LaunchShape L{};
+  size_t smem = 0;
+  bool tin_smem = false;
+  const int ov = layout_override();
+  if (use_tables && ov != 100 && nsym % 4 == 0 && vec_idx && vec_out) {
+    L = fast_shape(batch, dev_sms, spt);
+    const int64_t ring = (int64_t)(L.threads / 32) * L.lanes * POPF_RS * 16 * spt;
+    tin_smem = ntables <= 4096 && ring + ntables * 16 <= kSmemBudget;
+    const int64_t avail = kSmemBudget - ring - (tin_smem ? ntables * 16 : 0);
+    auto fits = [&](int t) {
+      switch (t) {
+        case TM_FUSED_SMEM: return popf_table_smem(t, ntables, fp, cdf_width, sstride) <= avail;
+        case TM_SPLIT_SMEM:
+          return lookup != TANS_LOOKUP_ALIAS && popf_table_smem(t, ntables, fp, cdf_width, sstride) <= avail;
+        case TM_CDF_SMEM:
+          return lookup == TANS_LOOKUP_SEARCH && popf_table_smem(t, ntables, fp, cdf_width, sstride) <= avail;
+        case TM_FUSED_GLOBAL: return lookup == TANS_LOOKUP_ALIAS && fused_bytes(ntables, fp) <= kFusedMaxBytes;
+        case TM_SPLIT_GLOBAL:
+          return lookup != TANS_LOOKUP_ALIAS && split_bytes(lookup, ntables, cdf_width, fp) <= kSplitMaxBytes;
+      }
+      return false;
+    };
+    if (ov >= 0 && fits(ov)) tm = ov;
+    else {
+      const int order[5] = {TM_FUSED_SMEM, TM_SPLIT_SMEM, TM_CDF_SMEM, TM_FUSED_GLOBAL, TM_SPLIT_GLOBAL};
+      for (int t : order)
+        if (fits(t)) {
+          tm = t;
+          break;
+        }
+    }
+    if (tm >= 0) smem = (size_t)ring + (tin_smem ? (size_t)ntables * 16 : 0) +
+                        (size_t)popf_table_smem(tm, ntables, fp, cdf_width, sstride);
+  }
+  const bool fast = tm >= 0;
+  const bool need_fused = fast ? (tm == TM_FUSED_SMEM || tm == TM_FUSED_GLOBAL)
+                               : (use_tables && ov != 100 && fused_bytes(ntables, fp) <= kFusedMaxBytes);
+  const bool need_split = fast && (tm == TM_SPLIT_SMEM || tm == TM_SPLIT_GLOBAL);
+
   size_t need = align_up((size_t)ntables * sizeof(TableInfo));
-  if (fused) need += align_up(((size_t)ntables << fp) * 4) + align_up(((size_t)ntables << fp) * 2);
+  if (need_fused) need += align_up((size_t)(ntables << fp) * 4) + align_up((size_t)(ntables << fp) * 2);
+  if (need_split) need += align_up((size_t)(ntables << fp) * 2) + align_up((size_t)ntables * sstride * 4);
   void* ws = workspace;
   bool owned = false;
   if (!ws) {
@@ -523,19 +499,7 @@ int pop_impl(int variant, int lookup, int interleave, int32_t* stream, int64_t b
   char* wsp = reinterpret_cast<char*>(ws);
   TableInfo* tinfo = reinterpret_cast<TableInfo*>(wsp);
   wsp += align_up((size_t)ntables * sizeof(TableInfo));
-  uint32_t* D = nullptr;
-  uint16_t* Sx = nullptr;
-  if (fused) {
-    D = reinterpret_cast<uint32_t*>(wsp);
-    wsp += align_up(((size_t)ntables << fp) * 4);
-    Sx = reinterpret_cast<uint16_t*>(wsp);
-  }
-  const int dev_sms = sm_count();
-  {
-    const int blocks = (int)std::min<int64_t>((ntables + 255) / 256, 4 * (int64_t)dev_sms);
-    build_table_info_kernel<<<blocks > 0 ? blocks : 1, 256, 0, s>>>(sizes, offsets, ntables, fp, tinfo);
-  }
-  PopParams P;
+  PopParams P{};
   P.stream = stream;
   P.batch = batch;
   P.width = width;
@@ -549,24 +513,52 @@ int pop_impl(int variant, int lookup, int interleave, int32_t* stream, int64_t b
   P.fp = fp;
   P.bp = bp;
   P.status = status;
-  P.vec = (reinterpret_cast<uintptr_t>(indexes) & 15u) == 0;
-  P.vec_out = (reinterpret_cast<uintptr_t>(out) & 15u) == 0;
-  P.fD = D;
-  P.fS = Sx;
-  const LaunchShape L = pick_launch(batch, dev_sms);
-  P.lanes = L.lanes;
-  const int64_t ring = (int64_t)L.threads * POP_RS * 16;
-  P.tin_smem = (ntables <= kPopTinfoSmemMax && ring + ntables * 16 <= kSmemBudget) ? 1 : 0;
-  P.fused_smem = (fused && ring + (P.tin_smem ? ntables * 16 : 0) + (ntables << fp) * 6 <= kSmemBudget) ? 1 : 0;
-  if (fused) {
-    if (variant == TANS_RANS64) launch_fused_build<0>(P, lookup, D, Sx, dev_sms, s);
-    else if (variant == TANS_RANS32) launch_fused_build<1>(P, lookup, D, Sx, dev_sms, s);
-    else launch_fused_build<2>(P, lookup, D, Sx, dev_sms, s);
+  P.vec = vec_idx;
+  P.vec_out = vec_out;
+  P.st_stride = sstride;
+  if (need_fused) {
+    P.fD = reinterpret_cast<uint32_t*>(wsp);
+    wsp += align_up((size_t)(ntables << fp) * 4);
+    P.fS = reinterpret_cast<uint16_t*>(wsp);
+  } else if (need_split) {
+    P.fS = reinterpret_cast<uint16_t*>(wsp);
+    wsp += align_up((size_t)(ntables << fp) * 2);
+    P.fST = reinterpret_cast<uint32_t*>(wsp);
   }
-  if (variant == TANS_RANS64) launch_pop_v<0>(P, lookup, bypass != 0, interleave, L, s);
-  else if (variant == TANS_RANS32) launch_pop_v<1>(P, lookup, bypass != 0, interleave, L, s);
-  else launch_pop_v<2>(P, lookup, bypass != 0, interleave, L, s);
+  {
+    const int blocks = (int)std::min<int64_t>((ntables + 255) / 256, 4 * (int64_t)dev_sms);
+    build_table_info_kernel<<<blocks > 0 ? blocks : 1, 256, 0, s>>>(sizes, offsets, ntables, fp, tinfo);
+  }
+  if (need_fused || need_split) {
+    uint32_t* D = const_cast<uint32_t*>(P.fD);
+    uint16_t* Sx = const_cast<uint16_t*>(P.fS);
+    uint32_t* ST = const_cast<uint32_t*>(P.fST);
+    if (variant == TANS_RANS64) build_tables<0>(P, lookup, need_fused, D, Sx, ST, dev_sms, s);
+    else if (variant == TANS_RANS32) build_tables<1>(P, lookup, need_fused, D, Sx, ST, dev_sms, s);
+    else build_tables<2>(P, lookup, need_fused, D, Sx, ST, dev_sms, s);
+  }
+  if (fast) {
+    P.lanes = L.lanes;
+    P.tin_smem = tin_smem ? 1 : 0;
+    P.spt = spt;
+    bool launched;
+    if (variant == TANS_RANS64) launched = launch_pop_fast<0>(P, lookup, bypass != 0, tm, spt, L.blocks, L.threads, smem, s);
+    else if (variant == TANS_RANS32) launched = launch_pop_fast<1>(P, lookup, bypass != 0, tm, spt, L.blocks, L.threads, smem, s);
+    else launched = launch_pop_fast<2>(P, lookup, bypass != 0, tm, spt, L.blocks, L.threads, smem, s);
+    if (!launched) rc = TANS_E_INVALID_ARGUMENT;
+  } else {
+    L = pick_launch(batch, dev_sms);
+    P.lanes = L.lanes;
+    const int64_t ring = (int64_t)L.threads * POP_RS * 16;
+    P.tin_smem = (ntables <= kPopTinfoSmemMax && ring + ntables * 16 <= kSmemBudget) ? 1 : 0;
+    P.fused_smem =
+        (P.fD && ring + (P.tin_smem ? ntables * 16 : 0) + (ntables << fp) * 6 <= kSmemBudget) ? 1 : 0;
+    if (variant == TANS_RANS64) launch_pop_v<0>(P, lookup, bypass != 0, interleave, L, s);
+    else if (variant == TANS_RANS32) launch_pop_v<1>(P, lookup, bypass != 0, interleave, L, s);
+    else launch_pop_v<2>(P, lookup, bypass != 0, interleave, L, s);
+  }
   if (owned) cudaFreeAsync(ws, s);
+  if (rc != TANS_OK) return rc;
   return cudaGetLastError() == cudaSuccess ? TANS_OK : TANS_E_CUDA;
 }
 
