@@ -281,7 +281,7 @@ def test_device_stream_helpers():
     assert same_rows(out.cpu().numpy(), d["pushed"])
 
 
-LAYOUTS = ["fused_smem", "split_smem", "cdf_smem", "fused_global", "split_global", "generic"]
+LAYOUTS = ["fused_smem", "split_smem", "fused_global", "split_global", "bucket_global", "generic"]
 
 
 @pytest.mark.parametrize("layout", LAYOUTS)
@@ -293,10 +293,8 @@ def test_fast_pop_layouts(C, layout, variant, lookup, bypass, spt, monkeypatch):
     """Aligned rows with a length divisible by 4 take the fast pop kernel; every table layout it
     can use is forced in turn (an infeasible one falls back to the automatic choice) and must
     decode exactly what the oracle decodes, with the same final stream rows."""
-    if layout in ("split_smem", "cdf_smem", "split_global") and lookup == "alias":
+    if layout in ("split_smem", "split_global", "bucket_global") and lookup == "alias":
         pytest.skip("alias offsets depend on cum: fused layouts only")
-    if layout == "cdf_smem" and lookup != "search":
-        pytest.skip("shared-memory bisection is the search lookup")
     if layout == "fused_global" and lookup != "alias" and spt == "4":
         pytest.skip("fused_global serves alias tables")
     monkeypatch.setenv("TORCH_ANS_B200_POP_LAYOUT", layout)

@@ -174,22 +174,30 @@ template <int N> __device__ __forceinline__ void cp_async_wait() {
 // once goes first (evict_first), so streaming rows do not push the tables out of L2.
 __device__ __forceinline__ unsigned long long policy_evict_last() {
   unsigned long long p;
-  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;\n" : "=l"(p));
+  asm("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;\n" : "=l"(p));
   return p;
 }
 __device__ __forceinline__ unsigned long long policy_evict_first() {
   unsigned long long p;
-  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;\n" : "=l"(p));
+  asm("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;\n" : "=l"(p));
   return p;
 }
+// (not volatile: these read data that no thread writes during the kernel, so the compiler may
+// hoist and interleave them like ordinary loads -- the independent chains of a thread then keep
+// several table loads in flight at once)
 __device__ __forceinline__ uint32_t ld_hint_u32(const uint32_t* p, unsigned long long policy) {
   uint32_t v;
-  asm volatile("ld.global.nc.L2::cache_hint.u32 %0, [%1], %2;\n" : "=r"(v) : "l"(p), "l"(policy));
+  asm("ld.global.nc.L2::cache_hint.u32 %0, [%1], %2;\n" : "=r"(v) : "l"(p), "l"(policy));
   return v;
 }
 __device__ __forceinline__ uint32_t ld_hint_u16(const uint16_t* p, unsigned long long policy) {
   unsigned short v;
-  asm volatile("ld.global.nc.L2::cache_hint.u16 %0, [%1], %2;\n" : "=h"(v) : "l"(p), "l"(policy));
+  asm("ld.global.nc.L2::cache_hint.u16 %0, [%1], %2;\n" : "=h"(v) : "l"(p), "l"(policy));
+  return v;
+}
+__device__ __forceinline__ unsigned long long ld_hint_u64(const unsigned long long* p, unsigned long long policy) {
+  unsigned long long v;
+  asm("ld.global.nc.L2::cache_hint.u64 %0, [%1], %2;\n" : "=l"(v) : "l"(p), "l"(policy));
   return v;
 }
 __device__ __forceinline__ void st_hint_v4(int4* p, int4 v, unsigned long long policy) {

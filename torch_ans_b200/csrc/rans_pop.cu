@@ -74,6 +74,62 @@ __global__ void build_split_s_kernel(const int32_t* cdfs, int64_t ntables, int64
   }
 }
 
+// Bucket table: one 8-byte entry per 16 consecutive cum values of a table, words
+//   w0 = s0 | two << 15, w1 = start of s0, w2 = (two ? start of s0+1 : freq of s0 mod 2^16),
+//   w3 = (two ? end of s0+1 mod 2^16 : 0)
+// where s0 is the symbol of the bucket's first cum and `two` says one more symbol starts inside
+// the bucket.  Every cum of the bucket is checked against the reference lookup; a bucket the
+// entry cannot reproduce exactly is marked w0 = 0xFFFF and decoded through the split tables.
+template <int V, int LK>
+__global__ void build_bucket_kernel(const int32_t* cdfs, int64_t ntables, int64_t cdf_width, const TableInfo* tinfo,
+                                    int fp, unsigned long long* BK) {
+  const int64_t nb = (int64_t)1 << (fp - kBucketBits), total = ntables * nb;
+  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t k = e / nb;
+    const int32_t lo = (int32_t)((e - k * nb) << kBucketBits);
+    const TableInfo t = tinfo[k];
+    const int32_t* row = cdfs + k * cdf_width;
+    unsigned long long out = 0xFFFFull;
+    int64_t s0 = 0;
+    int32_t off0 = 0, f0 = 0;
+    bool good = lookup_symbol<V, LK>(row, t, lo, cdf_width, fp, s0, off0, f0);
+    const int32_t start0 = lo - off0;
+    good = good && s0 >= 0 && s0 < 0x7FFF && start0 >= 0 && start0 <= 0xFFFF && f0 >= 1 && f0 <= 0x10000;
+    bool two = false;
+    int32_t c1 = 0, f1 = 0;
+    for (int i = 1; good && i < (1 << kBucketBits); ++i) {
+      int64_t s;
+      int32_t off, f;
+      const int32_t cum = lo + i;
+      if (!lookup_symbol<V, LK>(row, t, cum, cdf_width, fp, s, off, f)) {
+        good = false;
+        break;
+      }
+      const int32_t st = cum - off;
+      if (s == s0) {
+        good = !two && st == start0 && f == f0;
+      } else if (s == s0 + 1 && !two) {
+        two = true;
+        c1 = st;
+        f1 = f;
+        good = c1 == cum && c1 <= 0xFFFF && f1 >= 1 && f1 <= 0x10000;
+      } else {
+        good = two && s == s0 + 1 && st == c1 && f == f1;
+      }
+    }
+    if (good) {
+      const uint32_t w0 = (uint32_t)s0 | (two ? 0x8000u : 0u);
+      const uint32_t w2 = two ? (uint32_t)c1 : ((uint32_t)f0 & 0xFFFFu);
+      const uint32_t w3 = two ? ((uint32_t)(c1 + f1) & 0xFFFFu) : 0u;
+      // the start..stop difference of the last symbol of a `two` bucket must reproduce f0 too
+      if (!two || ((uint32_t)(c1 - start0) == (uint32_t)f0))
+        out = (unsigned long long)w0 | ((unsigned long long)start0 << 16) | ((unsigned long long)w2 << 32) |
+              ((unsigned long long)w3 << 48);
+    }
+    BK[e] = out;
+  }
+}
+
 __global__ void build_split_st_kernel(const int32_t* cdfs, int64_t ntables, int64_t cdf_width, int64_t st_stride,
                                       uint32_t* ST) {
   const int64_t total = ntables * st_stride;
@@ -309,6 +365,8 @@ static int64_t split_bytes(int lookup, int64_t ntables, int64_t cdf_width, int f
   return ntables * ((int64_t)2 << fp) + ntables * split_stride(lookup, cdf_width, fp) * 4;
 }
 
+static int64_t bucket_bytes(int64_t ntables, int fp) { return fp >= kBucketBits ? ntables * ((int64_t)8 << (fp - kBucketBits)) : 0; }
+
 static bool tables_enabled() {
   const char* e = std::getenv("TORCH_ANS_B200_FUSED");
   return !(e && e[0] == '0');
@@ -323,7 +381,8 @@ size_t pop_workspace_bytes(int variant, int lookup, int64_t ntables, int64_t cdf
       extra = align_up((size_t)(ntables << fp) * 4) + align_up((size_t)(ntables << fp) * 2);
     if (lookup != TANS_LOOKUP_ALIAS && split_bytes(lookup, ntables, cdf_width, fp) <= kSplitMaxBytes)
       extra = std::max(extra, align_up((size_t)(ntables << fp) * 2) +
-                                  align_up((size_t)ntables * split_stride(lookup, cdf_width, fp) * 4));
+                                  align_up((size_t)ntables * split_stride(lookup, cdf_width, fp) * 4) +
+                                  align_up((size_t)bucket_bytes(ntables, fp)));
     n += extra;
   }
   return n;
@@ -395,18 +454,25 @@ static void build_tables(const PopParams& P, int lookup, bool fused, uint32_t* D
 // launch shape of the fast kernel: streams spread over all SMs, up to 4 warps per SM, then up to
 // 4 streams per thread, then more lanes
 static LaunchShape fast_shape(int64_t streams, int sms, int& spt) {
+  // lanes of a warp run their chains in lockstep for free, so one stream per thread is the
+  // default; TORCH_ANS_B200_POP_WARPS / _LANES / _SPT override the shape for tuning
   LaunchShape L{1, 32, 1};
   const int64_t per_sm = (streams + sms - 1) / sms;
-  int64_t warps = std::min<int64_t>(4, per_sm);
-  int64_t sp = (per_sm + warps - 1) / warps;
-  sp = sp >= 4 ? 4 : (sp >= 2 ? 2 : 1);
+  int64_t sp = 1;
   const int spt_env = env_int("TORCH_ANS_B200_SPT", 0);
   if (spt_env == 1 || spt_env == 2 || spt_env == 4) sp = spt_env;
-  int64_t lanes = (per_sm + warps * sp - 1) / (warps * sp);
+  const int64_t threads_sm = (per_sm + sp - 1) / sp;
+  // measured on B200 (8,192 streams, 55 per SM): 16 warps x 4 lanes beat 4 x 14 by 1.3x, since a
+  // warp's step is one dependent L2 access and more warps per scheduler overlap those waits
+  int64_t warps = std::min<int64_t>(threads_sm, env_int("TORCH_ANS_B200_POP_WARPS", 16));
+  if (warps < 1) warps = 1;
+  int64_t lanes = (threads_sm + warps - 1) / warps;
   if (lanes > 32) {
     lanes = 32;
-    warps = std::min<int64_t>(4, (per_sm + 32 * sp - 1) / (32 * sp));
+    warps = std::min<int64_t>(16, (threads_sm + 31) / 32);
   }
+  const int lanes_env = env_int("TORCH_ANS_B200_POP_LANES", 0);
+  if (lanes_env > 0 && lanes_env <= 32) lanes = lanes_env;
   spt = (int)sp;
   L.lanes = (int)lanes;
   L.threads = (int)(warps * 32);
@@ -422,7 +488,7 @@ static int layout_override() {
   if (v == "fused_global") return TM_FUSED_GLOBAL;
   if (v == "split_smem") return TM_SPLIT_SMEM;
   if (v == "split_global") return TM_SPLIT_GLOBAL;
-  if (v == "cdf_smem") return TM_CDF_SMEM;
+  if (v == "bucket_global") return TM_BUCKET_GLOBAL;
   if (v == "generic") return 100;
   return -1;
 }
@@ -452,41 +518,47 @@ int pop_impl(int variant, int lookup, int interleave, int32_t* stream, int64_t b
   if (use_tables && ov != 100 && nsym % 4 == 0 && vec_idx && vec_out) {
     L = fast_shape(batch, dev_sms, spt);
     const int64_t ring = (int64_t)(L.threads / 32) * L.lanes * POPF_RS * 16 * spt;
-    tin_smem = ntables <= 4096 && ring + ntables * 16 <= kSmemBudget;
-    const int64_t avail = kSmemBudget - ring - (tin_smem ? ntables * 16 : 0);
+    tin_smem = true;  // the fast kernel always stages the per-table info
+    const int64_t avail = (ntables <= 4096) ? kSmemBudget - ring : -1;
     auto fits = [&](int t) {
       switch (t) {
         case TM_FUSED_SMEM: return popf_table_smem(t, ntables, fp, cdf_width, sstride) <= avail;
         case TM_SPLIT_SMEM:
           return lookup != TANS_LOOKUP_ALIAS && popf_table_smem(t, ntables, fp, cdf_width, sstride) <= avail;
-        case TM_CDF_SMEM:
-          return lookup == TANS_LOOKUP_SEARCH && popf_table_smem(t, ntables, fp, cdf_width, sstride) <= avail;
-        case TM_FUSED_GLOBAL: return lookup == TANS_LOOKUP_ALIAS && fused_bytes(ntables, fp) <= kFusedMaxBytes;
+        case TM_FUSED_GLOBAL:
+          return lookup == TANS_LOOKUP_ALIAS && popf_table_smem(t, ntables, fp, cdf_width, sstride) <= avail &&
+                 fused_bytes(ntables, fp) <= kFusedMaxBytes;
         case TM_SPLIT_GLOBAL:
-          return lookup != TANS_LOOKUP_ALIAS && split_bytes(lookup, ntables, cdf_width, fp) <= kSplitMaxBytes;
+          return lookup != TANS_LOOKUP_ALIAS && popf_table_smem(t, ntables, fp, cdf_width, sstride) <= avail &&
+                 split_bytes(lookup, ntables, cdf_width, fp) <= kSplitMaxBytes;
+        case TM_BUCKET_GLOBAL:
+          return lookup != TANS_LOOKUP_ALIAS && fp >= kBucketBits &&
+                 popf_table_smem(t, ntables, fp, cdf_width, sstride) <= avail &&
+                 split_bytes(lookup, ntables, cdf_width, fp) <= kSplitMaxBytes;
       }
       return false;
     };
     if (ov >= 0 && fits(ov)) tm = ov;
     else {
-      const int order[5] = {TM_FUSED_SMEM, TM_SPLIT_SMEM, TM_CDF_SMEM, TM_FUSED_GLOBAL, TM_SPLIT_GLOBAL};
+      const int order[5] = {TM_FUSED_SMEM, TM_SPLIT_SMEM, TM_FUSED_GLOBAL, TM_BUCKET_GLOBAL, TM_SPLIT_GLOBAL};
       for (int t : order)
         if (fits(t)) {
           tm = t;
           break;
         }
     }
-    if (tm >= 0) smem = (size_t)ring + (tin_smem ? (size_t)ntables * 16 : 0) +
-                        (size_t)popf_table_smem(tm, ntables, fp, cdf_width, sstride);
+    if (tm >= 0) smem = (size_t)ring + (size_t)popf_table_smem(tm, ntables, fp, cdf_width, sstride);
   }
   const bool fast = tm >= 0;
   const bool need_fused = fast ? (tm == TM_FUSED_SMEM || tm == TM_FUSED_GLOBAL)
                                : (use_tables && ov != 100 && fused_bytes(ntables, fp) <= kFusedMaxBytes);
-  const bool need_split = fast && (tm == TM_SPLIT_SMEM || tm == TM_SPLIT_GLOBAL);
+  const bool need_split = fast && (tm == TM_SPLIT_SMEM || tm == TM_SPLIT_GLOBAL || tm == TM_BUCKET_GLOBAL);
+  const bool need_bucket = fast && tm == TM_BUCKET_GLOBAL;
 
   size_t need = align_up((size_t)ntables * sizeof(TableInfo));
   if (need_fused) need += align_up((size_t)(ntables << fp) * 4) + align_up((size_t)(ntables << fp) * 2);
   if (need_split) need += align_up((size_t)(ntables << fp) * 2) + align_up((size_t)ntables * sstride * 4);
+  if (need_bucket) need += align_up((size_t)bucket_bytes(ntables, fp));
   void* ws = workspace;
   bool owned = false;
   if (!ws) {
@@ -524,6 +596,8 @@ int pop_impl(int variant, int lookup, int interleave, int32_t* stream, int64_t b
     P.fS = reinterpret_cast<uint16_t*>(wsp);
     wsp += align_up((size_t)(ntables << fp) * 2);
     P.fST = reinterpret_cast<uint32_t*>(wsp);
+    wsp += align_up((size_t)ntables * sstride * 4);
+    if (need_bucket) P.fBK = reinterpret_cast<unsigned long long*>(wsp);
   }
   {
     const int blocks = (int)std::min<int64_t>((ntables + 255) / 256, 4 * (int64_t)dev_sms);
@@ -536,6 +610,20 @@ int pop_impl(int variant, int lookup, int interleave, int32_t* stream, int64_t b
     if (variant == TANS_RANS64) build_tables<0>(P, lookup, need_fused, D, Sx, ST, dev_sms, s);
     else if (variant == TANS_RANS32) build_tables<1>(P, lookup, need_fused, D, Sx, ST, dev_sms, s);
     else build_tables<2>(P, lookup, need_fused, D, Sx, ST, dev_sms, s);
+  }
+  if (need_bucket) {
+    unsigned long long* BK = const_cast<unsigned long long*>(P.fBK);
+    const int64_t nbk = ntables << (fp - kBucketBits);
+    const int bb = (int)std::max<int64_t>(1, std::min<int64_t>((nbk + 127) / 128, 16 * (int64_t)dev_sms));
+    if (lookup == TANS_LOOKUP_INVCDF) {
+      if (variant == TANS_RANS64) build_bucket_kernel<0, LK_INVCDF><<<bb, 128, 0, s>>>(cdfs, ntables, cdf_width, tinfo, fp, BK);
+      else if (variant == TANS_RANS32) build_bucket_kernel<1, LK_INVCDF><<<bb, 128, 0, s>>>(cdfs, ntables, cdf_width, tinfo, fp, BK);
+      else build_bucket_kernel<2, LK_INVCDF><<<bb, 128, 0, s>>>(cdfs, ntables, cdf_width, tinfo, fp, BK);
+    } else {
+      if (variant == TANS_RANS64) build_bucket_kernel<0, LK_SEARCH><<<bb, 128, 0, s>>>(cdfs, ntables, cdf_width, tinfo, fp, BK);
+      else if (variant == TANS_RANS32) build_bucket_kernel<1, LK_SEARCH><<<bb, 128, 0, s>>>(cdfs, ntables, cdf_width, tinfo, fp, BK);
+      else build_bucket_kernel<2, LK_SEARCH><<<bb, 128, 0, s>>>(cdfs, ntables, cdf_width, tinfo, fp, BK);
+    }
   }
   if (fast) {
     P.lanes = L.lanes;

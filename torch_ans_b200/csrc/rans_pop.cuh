@@ -27,6 +27,7 @@ struct PopParams {
   const uint16_t* fS;  // symbol table S[k][cum] (fused and split layouts)
   const uint32_t* fST; // split layout: per-symbol {freq - 1, start} ST[k][s]
   int64_t st_stride;   // split layout: entries per table in ST
+  const unsigned long long* fBK;  // bucket layout: one entry per 16 cum values
   int spt;             // streams per thread (fast kernel)
   int fused_smem;      // fused table staged in shared memory
   int tin_smem;        // per-table info staged in shared memory

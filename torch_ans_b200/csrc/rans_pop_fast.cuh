@@ -11,7 +11,10 @@
 // own lookup, so every layout returns exactly what rans_pop_step would:
 //   TM_FUSED_SMEM / TM_FUSED_GLOBAL: D[k][cum] = (freq - 1) | (cum - start) << 16, S[k][cum] = s
 //   TM_SPLIT_SMEM / TM_SPLIT_GLOBAL: S[k][cum] = s, ST[k][s] = (freq - 1) | start << 16
-//   TM_CDF_SMEM: the cdf rows themselves in shared memory, bisection as in rans_utils.hpp:427-448
+//   TM_BUCKET_GLOBAL: one 8-byte entry per 16 cum values holding the bucket's first symbol, its
+//     start and at most one further boundary, so one load resolves (s, start, freq); buckets the
+//     entry cannot describe (verified per cum at build time) carry a marker and use the split
+//     tables, which are built alongside
 // S = 0xFFFF marks the entries the packed layouts cannot hold; those steps take the direct lookup.
 #pragma once
 
@@ -19,18 +22,20 @@
 
 namespace tans {
 
-enum : int { TM_FUSED_SMEM = 0, TM_FUSED_GLOBAL = 1, TM_SPLIT_SMEM = 2, TM_SPLIT_GLOBAL = 3, TM_CDF_SMEM = 4 };
+enum : int { TM_FUSED_SMEM = 0, TM_FUSED_GLOBAL = 1, TM_SPLIT_SMEM = 2, TM_SPLIT_GLOBAL = 3, TM_BUCKET_GLOBAL = 4 };
+constexpr int kBucketBits = 4;  // bucket layout: 16 cum values per bucket
 constexpr int POPF_RS = 8;  // index ring slots (chunks of 4)
 constexpr int POPF_L = 6;   // chunks between an index load and its use
 
 // bytes of shared memory the tables of a layout occupy
 inline int64_t popf_table_smem(int tm, int64_t ntables, int fp, int64_t cdf_width, int64_t st_stride) {
+  (void)cdf_width;
   const int64_t m = ntables << fp;
+  const int64_t info = ntables * 24;  // TableInfo + {offset, escape slot}
   switch (tm) {
-    case TM_FUSED_SMEM: return m * 4 + m * 2 + 16;
-    case TM_SPLIT_SMEM: return ntables * st_stride * 4 + m * 2 + 16;
-    case TM_CDF_SMEM: return ntables * cdf_width * 4;
-    default: return 0;
+    case TM_FUSED_SMEM: return info + m * 4 + m * 2 + 16;
+    case TM_SPLIT_SMEM: return info + ntables * st_stride * 4 + m * 2 + 16;
+    default: return info;
   }
 }
 
@@ -58,9 +63,73 @@ template <int V> struct FastCursor {
   }
 };
 
-template <int V, int LK, bool BYPASS, int TM, int SPT>
-__global__ void __launch_bounds__(128) pop_fast_kernel(const PopParams P) {
+// Exact handling of one symbol of one stream (every case the reference has: bad index, packed
+// table miss, escapes, underflow).  Used to replay a chunk the optimistic pass flagged.
+template <int V, int LK, bool BYPASS, int TM>
+__device__ __forceinline__ int32_t popf_exact(const PopParams& P, typename VT<V>::State& x, FastCursor<V>& cur,
+                                              int32_t k, const TableInfo* tsm, const uint32_t* tD, const uint16_t* tS,
+                                              unsigned long long pol_keep) {
   using S = typename VT<V>::State;
+  if ((uint32_t)k >= (uint64_t)P.ntables) {
+    cur.c.err |= DEV_BAD_INDEX;
+    return 0;
+  }
+  const TableInfo ti = P.tin_smem ? tsm[k] : load_tinfo(P.tinfo, k);
+  const uint32_t cum = (uint32_t)x & (uint32_t)(((int64_t)1 << P.fp) - 1);
+  const int64_t e = ((int64_t)k << P.fp) | cum;
+  bool fast = false;
+  int32_t sv = 0, off = 0, freq = 0;
+  if constexpr (TM == TM_FUSED_SMEM || TM == TM_FUSED_GLOBAL) {
+    uint32_t d, s16;
+    if constexpr (TM == TM_FUSED_SMEM) {
+      d = tD[e];
+      s16 = tS[e];
+    } else {
+      d = ld_hint_u32(P.fD + e, pol_keep);
+      s16 = ld_hint_u16(P.fS + e, pol_keep);
+    }
+    fast = s16 != 0xFFFFu;
+    sv = (int32_t)s16;
+    freq = (int32_t)(d & 0xFFFFu) + 1;
+    off = (int32_t)(d >> 16);
+  } else {
+    uint32_t s16, st = 0;
+    if constexpr (TM == TM_SPLIT_SMEM) {
+      s16 = tS[e];
+      fast = s16 != 0xFFFFu;
+      if (fast) st = tD[(int64_t)k * P.st_stride + s16];
+    } else {
+      s16 = ld_hint_u16(P.fS + e, pol_keep);
+      fast = s16 != 0xFFFFu;
+      if (fast) st = ld_hint_u32(P.fST + (int64_t)k * P.st_stride + s16, pol_keep);
+    }
+    sv = (int32_t)s16;
+    freq = (int32_t)(st & 0xFFFFu) + 1;
+    off = (int32_t)cum - (int32_t)(st >> 16);
+  }
+  int32_t v;
+  bool ok = true;
+  if (fast) {
+    x = (S)((x >> P.fp) * to_state<S>(freq) + to_state<S>(off));
+    cur.c.refill(x);
+    v = sv;
+    if constexpr (BYPASS) {
+      if (v == ti.size - 2) {
+        const int32_t raw = pop_escape<V>(x, cur.c, P.bp);
+        v = raw >> 1;
+        v = (raw & 1) ? (-v - 1) : (v + ti.size - 2);
+      }
+    }
+  } else {
+    v = pop_chain<V, LK, BYPASS>(P, x, cur.c, k, ti, ok);
+  }
+  return ok ? (int32_t)((uint32_t)v + (uint32_t)ti.offset) : 0;
+}
+
+template <int V, int LK, bool BYPASS, int TM, int SPT>
+__global__ void __launch_bounds__(512) pop_fast_kernel(const PopParams P) {
+  using S = typename VT<V>::State;
+  using W = typename VT<V>::Word;
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const int T = blockDim.x, tid = threadIdx.x;
   const int warps = T >> 5, warp = tid >> 5, lane = tid & 31;
@@ -68,14 +137,18 @@ __global__ void __launch_bounds__(128) pop_fast_kernel(const PopParams P) {
   const int at = warp * P.lanes + lane;
   int4* ring = reinterpret_cast<int4*>(smem_raw);
   TableInfo* tsm = reinterpret_cast<TableInfo*>(ring + POPF_RS * nact * SPT);
-  unsigned char* tab = reinterpret_cast<unsigned char*>(tsm + (P.tin_smem ? P.ntables : 0));
+  int2* tsm2 = reinterpret_cast<int2*>(tsm + P.ntables);  // {offset, escape slot} per table
+  unsigned char* tab = reinterpret_cast<unsigned char*>(tsm2 + P.ntables);
   const int64_t M = (int64_t)1 << P.fp;
   const int64_t m = P.ntables << P.fp;
-  uint32_t* tD = reinterpret_cast<uint32_t*>(tab);  // fused: D; split: ST; cdf: rows
+  uint32_t* tD = reinterpret_cast<uint32_t*>(tab);  // fused: D; split: ST
   uint16_t* tS = reinterpret_cast<uint16_t*>(
       tab + (TM == TM_FUSED_SMEM ? m * 4 : (TM == TM_SPLIT_SMEM ? P.ntables * P.st_stride * 4 : 0)));
-  if (P.tin_smem)
-    for (int64_t k = tid; k < P.ntables; k += T) tsm[k] = P.tinfo[k];
+  for (int64_t k = tid; k < P.ntables; k += T) {
+    const TableInfo ti = P.tinfo[k];
+    tsm[k] = ti;
+    tsm2[k] = make_int2(ti.offset, ti.size - 2);
+  }
   if constexpr (TM == TM_FUSED_SMEM) {
     for (int64_t i = tid; i < m; i += T) tD[i] = P.fD[i];
     for (int64_t i = tid; i < m; i += T) tS[i] = P.fS[i];
@@ -83,46 +156,50 @@ __global__ void __launch_bounds__(128) pop_fast_kernel(const PopParams P) {
     const int64_t n = P.ntables * P.st_stride;
     for (int64_t i = tid; i < n; i += T) tD[i] = P.fST[i];
     for (int64_t i = tid; i < m; i += T) tS[i] = P.fS[i];
-  } else if constexpr (TM == TM_CDF_SMEM) {
-    const int64_t n = P.ntables * P.cdf_width;
-    const uint32_t* src = reinterpret_cast<const uint32_t*>(P.cdfs);
-    for (int64_t i = tid; i < n; i += T) tD[i] = src[i];
   }
   __syncthreads();
   if (lane >= P.lanes) return;
 
+  // streams of this thread; slots past the batch shadow the thread's first stream (same reads,
+  // nothing written), so the arithmetic below stays free of per-stream branches
   const int64_t tg = ((int64_t)blockIdx.x * warps + warp) * P.lanes + lane;
+  if (tg * SPT >= P.batch) return;
   int64_t b[SPT];
   bool live[SPT];
   FastCursor<V> cur[SPT];
   S x[SPT];
-  int32_t* rows[SPT];
+  const W* pw[SPT];
+  int32_t pcap[SPT];
 #pragma unroll
   for (int j = 0; j < SPT; ++j) {
-    b[j] = tg * SPT + j;
-    live[j] = b[j] < P.batch;
-    const int64_t bb = live[j] ? b[j] : 0;
-    rows[j] = P.stream + bb * P.width;
-    cur[j].c.payload = reinterpret_cast<const uint8_t*>(rows[j] + 1);
-    cur[j].c.p = live[j] ? (int64_t)rows[j][0] / VT<V>::WBYTES - 1 : -1;
+    live[j] = tg * SPT + j < P.batch;
+    b[j] = live[j] ? tg * SPT + j : tg * SPT;
+    const int32_t* row = P.stream + b[j] * P.width;
+    cur[j].c.payload = reinterpret_cast<const uint8_t*>(row + 1);
+    cur[j].c.p = (int64_t)row[0] / VT<V>::WBYTES - 1;
     cur[j].c.first = VT<V>::SBYTES / VT<V>::WBYTES;
     cur[j].c.cap = (P.width - 1) * 4 / VT<V>::WBYTES;
     cur[j].c.err = 0;
-    x[j] = load_state<V>(rows[j], 0);
+    x[j] = load_state<V>(row, 0);
     cur[j].prime();
+    pw[j] = reinterpret_cast<const W*>(cur[j].c.payload);
+    pcap[j] = (int32_t)min(cur[j].c.cap - 1, (int64_t)0x7fffffff);
   }
-  if (!live[0]) return;
+  bool always_exact = false;  // a row whose length points past its end is replayed exactly
+#pragma unroll
+  for (int j = 0; j < SPT; ++j) always_exact |= cur[j].c.p >= cur[j].c.cap || cur[j].c.p > 0x7ffffff0;
   const unsigned long long pol_keep = policy_evict_last(), pol_stream = policy_evict_first();
   const uint32_t cmask = (uint32_t)(M - 1);
+  const uint32_t kmax = (uint32_t)(P.ntables - 1);
   const int64_t N = P.nsym;
   const int nch = (int)(N >> 2);
+  const int first = VT<V>::SBYTES / VT<V>::WBYTES;
 
   for (int t = 0; t < nch + POPF_L; ++t) {
     if (t < nch) {
       int4* slot = ring + ((int64_t)(t & (POPF_RS - 1)) * nact + at) * SPT;
 #pragma unroll
-      for (int j = 0; j < SPT; ++j)
-        if (live[j]) cp_async16_hint(slot + j, P.idx + b[j] * N + 4 * (int64_t)t, pol_stream);
+      for (int j = 0; j < SPT; ++j) cp_async16_hint(slot + j, P.idx + b[j] * N + 4 * (int64_t)t, pol_stream);
     }
     cp_async_commit();
     cp_async_wait<POPF_L - 1>();
@@ -130,6 +207,8 @@ __global__ void __launch_bounds__(128) pop_fast_kernel(const PopParams P) {
     if (cc < 0) continue;
     const int4* slot = ring + ((int64_t)(cc & (POPF_RS - 1)) * nact + at) * SPT;
     int32_t kv[SPT][4], ov[SPT][4];
+    S x0[SPT], w0[SPT];
+    int32_t p0[SPT];
 #pragma unroll
     for (int j = 0; j < SPT; ++j) {
       const int4 k4 = slot[j];
@@ -137,97 +216,123 @@ __global__ void __launch_bounds__(128) pop_fast_kernel(const PopParams P) {
       kv[j][1] = k4.y;
       kv[j][2] = k4.z;
       kv[j][3] = k4.w;
+      x0[j] = x[j];
+      w0[j] = cur[j].nextw;
+      p0[j] = (int32_t)cur[j].c.p;
     }
+    // ---- optimistic pass: straight-line code over the chunk's 4 x SPT steps
+    bool redo = always_exact;
+    if constexpr (!VT<V>::LOOP) {
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
+      for (int q = 0; q < 4; ++q) {
+        // phase 1: table loads of every stream (independent, all in flight together)
+        uint32_t kc[SPT], cum[SPT], sv[SPT], d[SPT];
+        unsigned long long bk[SPT];
+        bool fb[SPT];
+        int2 om[SPT];
+#pragma unroll
+        for (int j = 0; j < SPT; ++j) {
+          const int32_t k = kv[j][q];
+          kc[j] = min((uint32_t)k, kmax);
+          redo |= (uint32_t)k > kmax;
+          om[j] = tsm2[kc[j]];
+          cum[j] = (uint32_t)x[j] & cmask;
+          const int64_t e = ((int64_t)kc[j] << P.fp) | cum[j];
+          if constexpr (TM == TM_FUSED_SMEM) {
+            d[j] = tD[e];
+            sv[j] = tS[e];
+          } else if constexpr (TM == TM_FUSED_GLOBAL) {
+            d[j] = ld_hint_u32(P.fD + e, pol_keep);
+            sv[j] = ld_hint_u16(P.fS + e, pol_keep);
+          } else if constexpr (TM == TM_SPLIT_SMEM) {
+            sv[j] = tS[e];
+          } else if constexpr (TM == TM_BUCKET_GLOBAL) {
+            bk[j] = ld_hint_u64(P.fBK + (e >> kBucketBits), pol_keep);
+          } else {
+            sv[j] = ld_hint_u16(P.fS + e, pol_keep);
+          }
+        }
+        if constexpr (TM == TM_BUCKET_GLOBAL) {
+          // decode the bucket entries; marked buckets take the split tables (warp-uniform branch)
+          bool fb_any = false;
+#pragma unroll
+          for (int j = 0; j < SPT; ++j) {
+            const uint32_t w0 = (uint32_t)bk[j] & 0xFFFFu, start0 = (uint32_t)(bk[j] >> 16) & 0xFFFFu;
+            const uint32_t c1 = (uint32_t)(bk[j] >> 32) & 0xFFFFu, end1 = (uint32_t)(bk[j] >> 48);
+            fb[j] = w0 == 0xFFFFu;
+            fb_any |= fb[j];
+            const bool two = (w0 >> 15) != 0u;
+            const bool up = two && cum[j] >= c1;
+            const uint32_t s0 = w0 & 0x7FFFu;
+            sv[j] = s0 + (up ? 1u : 0u);
+            const uint32_t st0 = up ? c1 : start0;
+            const uint32_t stop = two ? (up ? end1 : c1) : (start0 + c1);
+            const uint32_t f = (stop - st0) & 0xFFFFu;
+            d[j] = ((f == 0u ? 0x10000u : f) - 1u) | (st0 << 16);
+          }
+          if (__any_sync(__activemask(), fb_any)) {
+#pragma unroll
+            for (int j = 0; j < SPT; ++j)
+              if (fb[j]) sv[j] = ld_hint_u16(P.fS + ((((int64_t)kc[j]) << P.fp) | cum[j]), pol_keep);
+#pragma unroll
+            for (int j = 0; j < SPT; ++j)
+              if (fb[j])
+                d[j] = ld_hint_u32(P.fST + (int64_t)kc[j] * P.st_stride + min(sv[j], (uint32_t)(P.st_stride - 1)),
+                                   pol_keep);
+          }
+        }
+        // phase 2 (split layouts): the per-symbol {freq, start} loads
+        if constexpr (TM == TM_SPLIT_SMEM || TM == TM_SPLIT_GLOBAL) {
+#pragma unroll
+          for (int j = 0; j < SPT; ++j) {
+            const int64_t si = (int64_t)kc[j] * P.st_stride + min(sv[j], (uint32_t)(P.st_stride - 1));
+            if constexpr (TM == TM_SPLIT_SMEM) d[j] = tD[si];
+            else d[j] = ld_hint_u32(P.fST + si, pol_keep);
+          }
+        }
+        // phase 3: state updates and refills
+#pragma unroll
+        for (int j = 0; j < SPT; ++j) {
+          uint32_t freq, off;
+          if constexpr (TM == TM_FUSED_SMEM || TM == TM_FUSED_GLOBAL) {
+            freq = (d[j] & 0xFFFFu) + 1u;
+            off = d[j] >> 16;
+          } else {  // split and bucket layouts: d = (freq - 1) | start << 16
+            freq = (d[j] & 0xFFFFu) + 1u;
+            off = cum[j] - (d[j] >> 16);
+          }
+          redo |= sv[j] == 0xFFFFu;
+          if constexpr (BYPASS) redo |= (int32_t)sv[j] == om[j].y;
+          x[j] = (S)((x[j] >> P.fp) * (S)freq + (S)off);
+          // single refill with the prefetched word; the next word is fetched at a clamped index
+          const bool r = (unsigned long long)x[j] < VT<V>::LB;
+          const int32_t pc = (int32_t)cur[j].c.p;
+          redo |= r && (pc < first);
+          x[j] = r ? (S)((x[j] << VT<V>::WB) | cur[j].nextw) : x[j];
+          const int32_t pn = pc - (r ? 1 : 0);
+          cur[j].c.p = pn;
+          if (r) cur[j].nextw = (S)__ldg(pw[j] + min(max(pn, 0), pcap[j]));
+          ov[j][q] = (int32_t)(sv[j] + (uint32_t)om[j].x);
+        }
+      }
+    } else {
+      redo = true;  // byte-word coder: several refills per step, always the exact path
+    }
+    if (redo) {
+      // ---- exact replay of this chunk from the saved states
 #pragma unroll
       for (int j = 0; j < SPT; ++j) {
-        ov[j][q] = 0;
-        if (!live[j]) continue;
-        const int32_t k = kv[j][q];
-        if ((uint32_t)k >= (uint64_t)P.ntables) {
-          cur[j].c.err |= DEV_BAD_INDEX;
-          continue;
-        }
-        const TableInfo ti = P.tin_smem ? tsm[k] : load_tinfo(P.tinfo, k);
-        const uint32_t cum = (uint32_t)x[j] & cmask;
-        bool fast = true;
-        int32_t sv = 0, off = 0, freq = 0;
-        if constexpr (TM == TM_FUSED_SMEM || TM == TM_FUSED_GLOBAL) {
-          const int64_t e = ((int64_t)k << P.fp) | cum;
-          uint32_t d, s16;
-          if constexpr (TM == TM_FUSED_SMEM) {
-            d = tD[e];
-            s16 = tS[e];
-          } else {
-            d = ld_hint_u32(P.fD + e, pol_keep);
-            s16 = ld_hint_u16(P.fS + e, pol_keep);
-          }
-          fast = s16 != 0xFFFFu;
-          sv = (int32_t)s16;
-          freq = (int32_t)(d & 0xFFFFu) + 1;
-          off = (int32_t)(d >> 16);
-        } else if constexpr (TM == TM_SPLIT_SMEM || TM == TM_SPLIT_GLOBAL) {
-          const int64_t e = ((int64_t)k << P.fp) | cum;
-          uint32_t s16, st = 0;
-          if constexpr (TM == TM_SPLIT_SMEM) {
-            s16 = tS[e];
-            fast = s16 != 0xFFFFu;
-            if (fast) st = tD[(int64_t)k * P.st_stride + s16];
-          } else {
-            s16 = ld_hint_u16(P.fS + e, pol_keep);
-            fast = s16 != 0xFFFFu;
-            if (fast) st = ld_hint_u32(P.fST + (int64_t)k * P.st_stride + s16, pol_keep);
-          }
-          sv = (int32_t)s16;
-          freq = (int32_t)(st & 0xFFFFu) + 1;
-          off = (int32_t)cum - (int32_t)(st >> 16);
-        } else {  // TM_CDF_SMEM: the reference's probe + bisection on the shared-memory row
-          const int32_t size = ti.size;
-          fast = size >= 2 && (int64_t)size <= P.cdf_width;
-          if (fast) {
-            const int32_t* row = reinterpret_cast<const int32_t*>(tD) + (int64_t)k * P.cdf_width;
-            S ix = to_state<S>((int32_t)((uint32_t)size * cum) >> P.fp);
-            uint32_t low = 0, high = (uint32_t)(size - 1);
-            while (high > low) {
-              if ((unsigned long long)ix >= (unsigned long long)size) {
-                fast = false;
-                break;
-              }
-              if ((int32_t)cum >= row[ix]) low = (uint32_t)ix + 1u;
-              else high = (uint32_t)ix;
-              ix = (S)((low + high) / 2u);
-            }
-            const int64_t s = (int64_t)(unsigned long long)(S)(ix - 1);
-            if (fast && s >= 0 && s < (int64_t)size - 1) {
-              sv = (int32_t)s;
-              const int32_t lo_c = row[s], hi_c = row[s + 1];
-              freq = (int32_t)((uint32_t)hi_c - (uint32_t)lo_c);
-              off = (int32_t)cum - lo_c;
-            } else {
-              fast = false;
-            }
-          }
-        }
-        int32_t v;
-        bool ok = true;
-        if (fast) {
-          x[j] = (S)((x[j] >> P.fp) * to_state<S>(freq) + to_state<S>(off));
-          cur[j].refill(x[j]);
-          v = sv;
-          if constexpr (BYPASS) {
-            if (v == ti.size - 2) {
-              const int32_t raw = pop_escape<V>(x[j], cur[j].c, P.bp);
-              v = raw >> 1;
-              v = (raw & 1) ? (-v - 1) : (v + ti.size - 2);
-              cur[j].prime();
-            }
-          }
-        } else {
-          v = pop_chain<V, LK, BYPASS>(P, x[j], cur[j].c, k, ti, ok);
+        x[j] = x0[j];
+        cur[j].nextw = w0[j];
+        cur[j].c.p = p0[j];
+      }
+#pragma unroll 1
+      for (int q = 0; q < 4; ++q) {
+#pragma unroll
+        for (int j = 0; j < SPT; ++j) {
+          ov[j][q] = popf_exact<V, LK, BYPASS, TM>(P, x[j], cur[j], kv[j][q], tsm, tD, tS, pol_keep);
           cur[j].prime();
         }
-        ov[j][q] = ok ? (int32_t)((uint32_t)v + (uint32_t)ti.offset) : 0;
       }
     }
 #pragma unroll
@@ -240,8 +345,9 @@ __global__ void __launch_bounds__(128) pop_fast_kernel(const PopParams P) {
 #pragma unroll
   for (int j = 0; j < SPT; ++j) {
     if (!live[j]) continue;
-    store_state<V>(rows[j], 0, x[j]);
-    rows[j][0] = (int32_t)((cur[j].c.p + 1) * VT<V>::WBYTES);
+    int32_t* row = P.stream + b[j] * P.width;
+    store_state<V>(row, 0, x[j]);
+    row[0] = (int32_t)((cur[j].c.p + 1) * VT<V>::WBYTES);
     report(P.status, cur[j].c.err);
   }
 }
@@ -278,16 +384,17 @@ bool popf_tm(const PopParams& P, int lookup, int tm, int spt, int blocks, int th
     return true;
   }
   if (lookup == 1) {
-    if (tm == TM_FUSED_SMEM) popf_spt<V, 1, BY, TM_FUSED_SMEM>(P, spt, blocks, threads, smem, s);
+    if (tm == TM_BUCKET_GLOBAL) popf_spt<V, 1, BY, TM_BUCKET_GLOBAL>(P, spt, blocks, threads, smem, s);
+    else if (tm == TM_FUSED_SMEM) popf_spt<V, 1, BY, TM_FUSED_SMEM>(P, spt, blocks, threads, smem, s);
     else if (tm == TM_SPLIT_SMEM) popf_spt<V, 1, BY, TM_SPLIT_SMEM>(P, spt, blocks, threads, smem, s);
     else if (tm == TM_SPLIT_GLOBAL) popf_spt<V, 1, BY, TM_SPLIT_GLOBAL>(P, spt, blocks, threads, smem, s);
     else return false;
     return true;
   }
-  if (tm == TM_FUSED_SMEM) popf_spt<V, 0, BY, TM_FUSED_SMEM>(P, spt, blocks, threads, smem, s);
+  if (tm == TM_BUCKET_GLOBAL) popf_spt<V, 0, BY, TM_BUCKET_GLOBAL>(P, spt, blocks, threads, smem, s);
+  else if (tm == TM_FUSED_SMEM) popf_spt<V, 0, BY, TM_FUSED_SMEM>(P, spt, blocks, threads, smem, s);
   else if (tm == TM_SPLIT_SMEM) popf_spt<V, 0, BY, TM_SPLIT_SMEM>(P, spt, blocks, threads, smem, s);
   else if (tm == TM_SPLIT_GLOBAL) popf_spt<V, 0, BY, TM_SPLIT_GLOBAL>(P, spt, blocks, threads, smem, s);
-  else if (tm == TM_CDF_SMEM) popf_spt<V, 0, BY, TM_CDF_SMEM>(P, spt, blocks, threads, smem, s);
   else return false;
   return true;
 }
