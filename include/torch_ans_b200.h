@@ -85,6 +85,25 @@ int tans_push(int variant, int use_alias, int num_interleaves,
               int freq_precision, int bypass_coding, int bypass_precision,
               void* workspace, size_t workspace_bytes, uint32_t* dev_status, void* cuda_stream);
 
+/* tans_push without any device allocation, for callers that cannot allocate device memory
+ * (hosts whose memory is owned by another allocator or budget, plugins that may only use the
+ * buffers they are handed, serving loops that must not allocate after start-up).  This entry
+ * point has no counterpart in the reference.  Arguments and results are those of tans_push; the
+ * encode-table scratch comes from a fixed 8 MiB array inside the library (held on every GPU that
+ * loads it until the process exits), so the table list must satisfy
+ * tans_push_workspace_size(variant, num_tables, cdf_width) <= 8 MiB (about 524,000 table
+ * entries), else TANS_E_TOO_LARGE is returned and nothing runs.  The first call on a device looks
+ * up the array's device address (cudaGetSymbolAddress); make that first call before any stream
+ * capture.  All calls share the array: calls whose GPU work may overlap (different streams,
+ * unordered threads) must be serialised by the caller. */
+int tans_push_noalloc(int variant, int use_alias, int num_interleaves,
+                      int32_t* stream, int64_t batch, int64_t stream_width,
+                      const int32_t* symbols, const int32_t* indexes, int64_t num_symbols,
+                      const int32_t* cdfs, int64_t num_tables, int64_t cdf_width,
+                      const int32_t* cdf_sizes, const int32_t* offsets,
+                      int freq_precision, int bypass_coding, int bypass_precision,
+                      uint32_t* dev_status, void* cuda_stream);
+
 /* Bytes of device scratch that tans_pop needs (per-table size/offset pairs and, for the lookup
  * tables it builds, their device copies). */
 size_t tans_pop_workspace_size(int variant, int lookup, int64_t num_tables, int64_t cdf_width,

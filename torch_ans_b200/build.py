@@ -27,7 +27,8 @@ INCLUDE = os.path.join(ROOT, "include")
 BUILD_DIR = os.path.join(PKG, "_build")
 LIB = os.path.join(PKG, "libtorch_ans_b200.so")
 CU_SOURCES = ["rans_push.cu", "rans_pop.cu", "rans_aux.cu", "rans_pop_fast_v0.cu", "rans_pop_fast_v1.cu",
-              "rans_pop_fast_v2.cu", "rans_push_fast_v0.cu", "rans_push_fast_v1.cu", "rans_push_fast_v2.cu"]
+              "rans_pop_fast_v2.cu", "rans_push_fast_v0.cu", "rans_push_fast_v1.cu", "rans_push_fast_v2.cu",
+              "rans_noalloc.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

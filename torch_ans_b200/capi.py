@@ -26,6 +26,7 @@ _SIGS = {
     "tans_status_string": ([_I], ctypes.c_char_p),
     "tans_push_workspace_size": ([_I, _I64, _I64], _SZ),
     "tans_push": ([_I, _I, _I, _P, _I64, _I64, _P, _P, _I64, _P, _I64, _I64, _P, _P, _I, _I, _I, _P, _SZ, _P, _P], _I),
+    "tans_push_noalloc": ([_I, _I, _I, _P, _I64, _I64, _P, _P, _I64, _P, _I64, _I64, _P, _P, _I, _I, _I, _P, _P], _I),
     "tans_pop_workspace_size": ([_I, _I, _I64, _I64, _I], _SZ),
     "tans_pop": ([_I, _I, _I, _P, _I64, _I64, _P, _P, _I64, _P, _I64, _I64, _P, _P, _I, _I, _I, _P, _SZ, _P, _P], _I),
     "tans_stream_max_length": ([_P, _I64, _I64, _P, _P], _I),
