@@ -52,12 +52,20 @@ extern "C" {
 #define TANS_DEV_UNDERFLOW 8u
 #define TANS_DEV_BAD_FREQ 16u
 #define TANS_DEV_BAD_ESCAPE 32u
+/* A kernel whose warps hand work to one another gave up waiting (every such wait is bounded);
+ * the rows of that call are not valid.  Not expected in normal operation. */
+#define TANS_DEV_STALLED 64u
 
 /* Library version, (major << 16) | (minor << 8) | patch. */
 int tans_version(void);
 
 /* Human-readable name of a return code. */
 const char* tans_status_string(int code);
+
+/* Number of kernels this library has launched in this process so far (all devices and streams).
+ * A diagnostic with no counterpart in the reference: benchmarks read it around a timed region to
+ * report how many of the library's kernels ran in it. */
+uint64_t tans_launch_count(void);
 
 /* Bytes of device scratch that tans_push needs for a table list of num_tables rows of cdf_width
  * entries (a per-entry reciprocal table plus per-table size/offset pairs). */

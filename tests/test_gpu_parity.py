@@ -289,14 +289,19 @@ LAYOUTS = ["fused_smem", "split_smem", "fused_global", "split_global", "bucket_g
 @pytest.mark.parametrize("lookup", ["search", "invcdf", "alias"])
 @pytest.mark.parametrize("bypass", [False, True])
 @pytest.mark.parametrize("spt", ["1", "4"])
-def test_fast_pop_layouts(C, layout, variant, lookup, bypass, spt, monkeypatch):
-    """Aligned rows with a length divisible by 4 take the fast pop kernel; every table layout it
+@pytest.mark.parametrize("kernel", ["lean", "fast"])
+def test_fast_pop_layouts(C, layout, variant, lookup, bypass, spt, kernel, monkeypatch):
+    """Aligned rows with a length divisible by 4 take the lean pop kernel (one stream per thread,
+    shortest serial step) or the fast one (several streams per thread); every table layout they
     can use is forced in turn (an infeasible one falls back to the automatic choice) and must
     decode exactly what the oracle decodes, with the same final stream rows."""
     if layout in ("split_smem", "split_global", "bucket_global") and lookup == "alias":
         pytest.skip("alias offsets depend on cum: fused layouts only")
     if layout == "fused_global" and lookup != "alias" and spt == "4":
         pytest.skip("fused_global serves alias tables")
+    if kernel == "lean" and spt == "4":
+        pytest.skip("the lean kernel runs one stream per thread")
+    monkeypatch.setenv("TORCH_ANS_B200_POP_KERNEL", kernel)
     monkeypatch.setenv("TORCH_ANS_B200_POP_LAYOUT", layout)
     monkeypatch.setenv("TORCH_ANS_B200_SPT", spt)
     rng = np.random.default_rng(zlib.crc32(f"fast-{layout}-{variant}-{lookup}-{bypass}-{spt}".encode()))
@@ -336,4 +341,173 @@ def test_fast_pop_layouts(C, layout, variant, lookup, bypass, spt, monkeypatch):
     dec = getattr(C, pop)(st, t(idx), t(pop_c), t(sizes), t(offs), **kw)
     assert C.device_status() == 0
     assert np.array_equal(dec.cpu().numpy(), sym)
+    assert same_rows(st.cpu().numpy(), ref_pop)
+
+
+PUSH_KERNELS = ["ws", "chunk", "generic"]
+
+
+def _push_case(rng, variant, alias, bypass, B, N):
+    """Tables and symbols for a push-kernel test: random cdfs (with escapes when `bypass`), or
+    alias remap rows."""
+    if alias:
+        fp, K, sp = 12, 3, 5
+        A = 1 << sp
+        pm = rng.random((K, A)) + 0.05
+        cdfs = O.pmf_to_quantized_cdf((pm / pm.sum(1, keepdims=True)).astype(np.float32), fp)
+        sizes = np.full(K, A + 1, np.int32)
+        offs = rng.integers(-3, 3, K).astype(np.int32)
+        push_c, _, ok = O.alias_build_table(cdfs, sizes, sp, fp)
+        assert ok == K
+        lo, hi = (-5, A + 5) if bypass else (0, A)
+    else:
+        fp, cdfs, sizes, offs = _random_case(rng, variant, bypass, K=6, A=30)
+        push_c = cdfs
+        A = cdfs.shape[1] - 2
+        lo, hi = (-20, A + 20) if bypass else (0, A + 1)
+    K = cdfs.shape[0]
+    idx = rng.integers(0, K, (B, N)).astype(np.int32)
+    sym = rng.integers(lo, hi, (B, N)).astype(np.int32)
+    if not bypass:
+        sym = (np.clip(sym, 0, sizes[idx] - 2) + offs[idx]).astype(np.int32)
+    return fp, push_c, sizes, offs, sym, idx
+
+
+@pytest.mark.parametrize("kernel", PUSH_KERNELS)
+@pytest.mark.parametrize("variant", VARIANTS)
+@pytest.mark.parametrize("alias", [False, True])
+@pytest.mark.parametrize("bypass", [False, True])
+@pytest.mark.parametrize("shape", [(3, 4), (45, 1000), (700, 252)])
+def test_fast_push_kernels(C, kernel, variant, alias, bypass, shape, monkeypatch):
+    """Aligned rows with a length divisible by 4 take a fast push kernel: the warp-specialised one
+    ("ws": chain warps fed by prep warps through a shared-memory ring), the single-role one
+    ("chunk") or the generic one, forced in turn.  Each must write exactly the oracle's rows
+    (length, state, words), with stream counts that leave blocks and warps partly filled and
+    lengths that leave the last group of chunks partial."""
+    monkeypatch.setenv("TORCH_ANS_B200_PUSH_KERNEL", kernel)
+    B, N = shape
+    rng = np.random.default_rng(zlib.crc32(f"pushk-{kernel}-{variant}-{alias}-{bypass}-{B}-{N}".encode()))
+    fp, push_c, sizes, offs, sym, idx = _push_case(rng, variant, alias, bypass, B, N)
+    ref, perr = O.push(variant, O.init_stream(variant, B), sym, idx, push_c, sizes, offs, fp, bypass, 4, alias=alias)
+    assert perr == 0
+    kw = dict(freq_precision=fp, bypass_coding=bypass, bypass_precision=4)
+    st = getattr(C, f"{variant}_init_stream")(B).cuda()
+    getattr(C, f"{variant}_alias_push" if alias else f"{variant}_push")(st, t(sym), t(idx), t(push_c), t(sizes),
+                                                                          t(offs), **kw)
+    assert C.device_status() == 0
+    assert same_rows(st.cpu().numpy(), ref)
+
+
+@pytest.mark.parametrize("streams_per_block,chain_warps,prep_warps",
+                         [("1", "1", "1"), ("64", "4", "4"), ("128", "4", "2"), ("37", "8", "8"), ("96", "2", "1")])
+@pytest.mark.parametrize("variant", VARIANTS)
+def test_ws_push_block_shapes(C, streams_per_block, chain_warps, prep_warps, variant, monkeypatch):
+    """The warp-specialised push with forced block shapes (streams per block, chain and prep warp
+    counts): one lane per stream on up to 8 chain warps, prep tasks shared unevenly among the prep
+    threads.  Rows must match the oracle's exactly."""
+    monkeypatch.setenv("TORCH_ANS_B200_PUSH_KERNEL", "ws")
+    monkeypatch.setenv("TORCH_ANS_B200_PUSHWS_STREAMS", streams_per_block)
+    monkeypatch.setenv("TORCH_ANS_B200_PUSHWS_CHAIN_WARPS", chain_warps)
+    monkeypatch.setenv("TORCH_ANS_B200_PUSHWS_PREP_WARPS", prep_warps)
+    B, N = 300, 404
+    rng = np.random.default_rng(zlib.crc32(f"wsshape-{streams_per_block}-{chain_warps}-{variant}".encode()))
+    fp, push_c, sizes, offs, sym, idx = _push_case(rng, variant, False, True, B, N)
+    ref, perr = O.push(variant, O.init_stream(variant, B), sym, idx, push_c, sizes, offs, fp, True, 4)
+    assert perr == 0
+    st = getattr(C, f"{variant}_init_stream")(B).cuda()
+    getattr(C, f"{variant}_push")(st, t(sym), t(idx), t(push_c), t(sizes), t(offs), freq_precision=fp,
+                                  bypass_coding=True, bypass_precision=4)
+    assert C.device_status() == 0
+    assert same_rows(st.cpu().numpy(), ref)
+
+
+@pytest.mark.parametrize("kernel", PUSH_KERNELS)
+@pytest.mark.parametrize("variant", VARIANTS)
+def test_push_row_overflow_matches_oracle(kernel, variant, monkeypatch):
+    """Rows too short for their words (a caller-sized buffer through the C ABI): every kernel keeps
+    the words that fit, counts the rest, flags TANS_DEV_OVERFLOW and never writes past the row,
+    exactly as the oracle's bounds-checked restatement does."""
+    from torch_ans_b200 import capi
+    monkeypatch.setenv("TORCH_ANS_B200_PUSH_KERNEL", kernel)
+    lib = capi.load()
+    B, N = 40, 400
+    rng = np.random.default_rng(zlib.crc32(f"ovf-{kernel}-{variant}".encode()))
+    fp, push_c, sizes, offs, sym, idx = _push_case(rng, variant, False, False, B, N)
+    init = O.init_stream(variant, B)
+    W = init.shape[1] + 6  # room for a few words only
+    host = np.zeros((B, W), np.int32)
+    host[:, : init.shape[1]] = init
+    ref = host.copy()
+    err = O.lib().orc_push(O.VARIANTS[variant], 0, 1, O._ptr(ref), B, W, O._ptr(sym), O._ptr(idx), N,
+                           O._ptr(push_c), push_c.shape[0], push_c.shape[1], O._ptr(sizes), O._ptr(offs), fp, 0, 4, 1)
+    assert err & O.ERR_OVERFLOW
+    # rows are contiguous, so a write past a row's end would land in the next row's length word;
+    # guard words after the last row catch the rest
+    guard = 8
+    flat = torch.full((B * W + guard,), 0x5A5A5A5A, dtype=torch.int32, device="cuda")
+    flat[: B * W] = t(host).reshape(-1)
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    cs = torch.cuda.current_stream().cuda_stream
+    s_d, i_d, c_d, z_d, o_d = t(sym), t(idx), t(push_c), t(sizes), t(offs)
+    rc = lib.tans_push(capi.VARIANT[variant], 0, 1, flat.data_ptr(), B, W, s_d.data_ptr(), i_d.data_ptr(), N,
+                       c_d.data_ptr(), c_d.shape[0], c_d.shape[1], z_d.data_ptr(), o_d.data_ptr(), fp, 0, 4, None, 0,
+                       status.data_ptr(), cs)
+    assert rc == 0
+    torch.cuda.synchronize()
+    assert status.item() == err
+    out = flat.cpu().numpy()
+    assert np.all(out[B * W:] == 0x5A5A5A5A)
+    assert np.array_equal(out[: B * W].reshape(B, W), ref)
+
+
+def _heavy_tail_case(rng, K=6, A=300, fp=16):
+    """Tables where most symbols have frequency 1 (long flat tails around a few large symbols), so
+    many 16-cum buckets hold more than two symbols and the bucket layout falls back per step."""
+    freqs = np.ones((K, A), np.int64)
+    for k in range(K):
+        big = rng.choice(A, 3, replace=False)
+        share = rng.dirichlet(np.ones(3)) * ((1 << fp) - A)
+        freqs[k, big] += np.floor(share).astype(np.int64)
+        freqs[k, big[0]] += (1 << fp) - freqs[k].sum()
+    cdfs = np.concatenate([np.zeros((K, 1), np.int64), np.cumsum(freqs, 1)], 1).astype(np.int32)
+    sizes = np.full(K, A + 1, np.int32)
+    offs = rng.integers(-8, 8, K).astype(np.int32)
+    return fp, cdfs, sizes, offs
+
+
+@pytest.mark.parametrize("kernel", ["lean", "fast"])
+@pytest.mark.parametrize("layout", ["bucket_global", "split_global", "split_smem", "fused_smem"])
+@pytest.mark.parametrize("lookup", ["search", "invcdf"])
+@pytest.mark.parametrize("variant", VARIANTS)
+def test_pop_heavy_tails_and_overrun(C, kernel, layout, lookup, variant, monkeypatch):
+    """Unit-frequency tails (bucket entries that cannot describe their cum range, so those steps
+    take the split tables or the exact step), symbols drawn uniformly over the alphabet (every
+    tail symbol occurs), bad table indexes in the pop, and pops that run past the encoded words
+    (underflow): outputs, final rows and error bits must all equal the oracle's."""
+    monkeypatch.setenv("TORCH_ANS_B200_POP_KERNEL", kernel)
+    monkeypatch.setenv("TORCH_ANS_B200_POP_LAYOUT", layout)
+    rng = np.random.default_rng(zlib.crc32(f"tail-{kernel}-{layout}-{lookup}-{variant}".encode()))
+    fp = 11 if layout.endswith("smem") else 16
+    if variant == "rans32_16":
+        fp = min(fp, 15)
+    fp, cdfs, sizes, offs = _heavy_tail_case(rng, A=200 if fp < 16 else 300, fp=fp)
+    pop_c = np.concatenate([cdfs, O.inverse_quantized_cdf(cdfs, fp)], 1) if lookup == "invcdf" else cdfs
+    K = cdfs.shape[0]
+    B, N, extra = 50, 600, 8
+    idx = rng.integers(0, K, (B, N)).astype(np.int32)
+    sym = (rng.integers(0, sizes[idx] - 1) + offs[idx]).astype(np.int32)
+    ref, perr = O.push(variant, O.init_stream(variant, B), sym, idx, cdfs, sizes, offs, fp, False)
+    assert perr == 0
+    # pop N + extra symbols with a few invalid indexes sprinkled in
+    idx_pop = np.concatenate([idx, rng.integers(0, K, (B, extra)).astype(np.int32)], 1)
+    bad = rng.random(idx_pop.shape) < 0.002
+    idx_pop[bad] = K + 3
+    ref_pop = ref.copy()
+    dec_ref, derr = O.pop(variant, ref_pop, idx_pop, pop_c, sizes, offs, fp, False, lookup=lookup)
+    assert derr & O.ERR_UNDERFLOW
+    st = t(ref)
+    dec = getattr(C, op_names(variant, 1, False, lookup)[1])(st, t(idx_pop), t(pop_c), t(sizes), t(offs),
+                                                           freq_precision=fp, bypass_coding=False)
+    assert C.device_status() == derr
+    assert np.array_equal(dec.cpu().numpy(), dec_ref)
     assert same_rows(st.cpu().numpy(), ref_pop)

@@ -19,11 +19,13 @@ LOOKUP = {"search": LOOKUP_SEARCH, "invcdf": LOOKUP_INVCDF, "alias": LOOKUP_ALIA
 
 OK = 0
 DEV_BAD_INDEX, DEV_BAD_VALUE, DEV_OVERFLOW, DEV_UNDERFLOW, DEV_BAD_FREQ, DEV_BAD_ESCAPE = 1, 2, 4, 8, 16, 32
+DEV_STALLED = 64
 
 _P, _I64, _I, _SZ = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_size_t
 _SIGS = {
     "tans_version": ([], _I),
     "tans_status_string": ([_I], ctypes.c_char_p),
+    "tans_launch_count": ([], ctypes.c_uint64),
     "tans_push_workspace_size": ([_I, _I64, _I64], _SZ),
     "tans_push": ([_I, _I, _I, _P, _I64, _I64, _P, _P, _I64, _P, _I64, _I64, _P, _P, _I, _I, _I, _P, _SZ, _P, _P], _I),
     "tans_push_noalloc": ([_I, _I, _I, _P, _I64, _I64, _P, _P, _I64, _P, _I64, _I64, _P, _P, _I, _I, _I, _P, _P], _I),

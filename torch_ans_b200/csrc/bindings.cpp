@@ -580,4 +580,6 @@ PYBIND11_MODULE(_C, m) {
   m.def("set_sync_check", [](bool on) { g_force_check = on; }, py::arg("enabled"),
         "Synchronise after every coding op and raise if a kernel reported an error.");
   m.def("library_version", []() { return tans_version(); });
+  m.def("launch_count", []() { return (uint64_t)tans_launch_count(); },
+        "kernels launched by the library in this process so far");
 }

@@ -20,6 +20,9 @@ struct LaunchShape {
 
 constexpr int kMaxWarpsPerBlock = 8;
 
+// count one kernel launch of this library (read back by tans_launch_count)
+void note_launch();
+
 inline int env_int(const char* name, int dflt) {
   const char* s = std::getenv(name);
   if (!s || !*s) return dflt;

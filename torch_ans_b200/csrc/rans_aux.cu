@@ -3,6 +3,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <mutex>
 
 #include "../../include/torch_ans_b200.h"
@@ -10,6 +11,10 @@
 #include "rans_host.h"
 
 namespace tans {
+
+static std::atomic<unsigned long long> g_launches{0};
+
+void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
 int sm_count() {
   static std::mutex mu;
@@ -150,6 +155,7 @@ extern "C" int tans_stream_max_length(const int32_t* stream, int64_t batch, int6
   if (batch < 0 || !out_max || (batch > 0 && (!stream || stream_width < 1))) return TANS_E_INVALID_ARGUMENT;
   tans::max_length_kernel<<<1, 1024, 0, reinterpret_cast<cudaStream_t>(cuda_stream)>>>(stream, batch, stream_width,
                                                                                        out_max);
+  tans::note_launch();
   return cudaGetLastError() == cudaSuccess ? TANS_OK : TANS_E_CUDA;
 }
 
@@ -165,6 +171,7 @@ extern "C" int tans_init_stream(int variant, int num_interleaves, int32_t* strea
   if (variant == TANS_RANS64) tans::init_stream_kernel<0><<<blocks, 256, 0, s>>>(stream, batch, stream_width, num_interleaves);
   else if (variant == TANS_RANS32) tans::init_stream_kernel<1><<<blocks, 256, 0, s>>>(stream, batch, stream_width, num_interleaves);
   else tans::init_stream_kernel<2><<<blocks, 256, 0, s>>>(stream, batch, stream_width, num_interleaves);
+  tans::note_launch();
   return cudaGetLastError() == cudaSuccess ? TANS_OK : TANS_E_CUDA;
 }
 
@@ -179,6 +186,7 @@ extern "C" int tans_gather_payloads(const int32_t* stream, int64_t batch, int64_
   const int blocks = (int)std::min<int64_t>(batch, 65535);
   tans::gather_payloads_kernel<<<blocks, 256, 0, reinterpret_cast<cudaStream_t>(cuda_stream)>>>(
       stream, batch, stream_width, record_offsets, prefix_bytes, prefix_rows, out);
+  tans::note_launch();
   return cudaGetLastError() == cudaSuccess ? TANS_OK : TANS_E_CUDA;
 }
 
@@ -190,6 +198,7 @@ extern "C" int tans_scatter_payloads(const uint8_t* in, const int64_t* payload_o
   const int blocks = (int)std::min<int64_t>(batch, 65535);
   tans::scatter_payloads_kernel<<<blocks, 256, 0, reinterpret_cast<cudaStream_t>(cuda_stream)>>>(
       in, payload_offsets, lengths, stream, batch, stream_width);
+  tans::note_launch();
   return cudaGetLastError() == cudaSuccess ? TANS_OK : TANS_E_CUDA;
 }
 
@@ -200,5 +209,8 @@ extern "C" int tans_cdf_fix_zero_freqs(int32_t* cdfs, int64_t rows, int64_t n, u
   if (!cdfs) return TANS_E_INVALID_ARGUMENT;
   const int blocks = (int)std::min<int64_t>((rows + 127) / 128, 4 * (int64_t)tans::sm_count());
   tans::cdf_fix_kernel<<<blocks, 128, 0, reinterpret_cast<cudaStream_t>(cuda_stream)>>>(cdfs, rows, n, dev_status);
+  tans::note_launch();
   return cudaGetLastError() == cudaSuccess ? TANS_OK : TANS_E_CUDA;
 }
+
+extern "C" uint64_t tans_launch_count(void) { return (uint64_t)tans::g_launches.load(std::memory_order_relaxed); }

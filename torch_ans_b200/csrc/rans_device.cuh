@@ -10,14 +10,14 @@
 //
 // The division x / freq of the push is done with an exact multiply-high by a precomputed
 // reciprocal (Granlund & Montgomery, "Division by invariant integers using multiplication",
-// PLDI 1994, Thm 4.2): for a divisor 2 <= d <= 2^31 with l = ceil(log2 d) and
-// m = ceil(2^(N+l) / d) < 2^W, floor(n / d) = mulhi_W(n, m) >> (l - 1) for every n < 2^N, where
+// PLDI 1994, Thm 4.2): for a divisor 1 <= d <= 2^31 with l = ceil(log2 d) and
+// m = ceil(2^(N+l) / d) <= 2^W, floor(n / d) = floor(n * m / 2^(N+l)) for every n < 2^N, where
 // (N, W) = (63, 64) for the 64-bit state and (31, 32) for the 32-bit states.  Proof: m*d =
 // 2^(N+l) + e with 0 <= e < d <= 2^l, so n*m / 2^(N+l) = n/d + n*e/(d*2^(N+l)) and the second
-// term is < 1/d; since n/d = floor(n/d) + j/d with j <= d-1 the floor is unchanged.  The push
-// only divides a renormalised state, which is < freq * 2^(state_bits-1-fp) <= 2^N (or a
-// word-shifted state < 2^(state_bits-word_bits)), so the precondition n < 2^N always holds.
-// d = 1 is handled by a select (q = n).
+// term is < 1/d; since n/d = floor(n/d) + j/d with j <= d-1 the floor is unchanged.  m fits in
+// W bits (m < 2^W for d >= 3, m = 2^N for d = 1 and 2), and floor(n*m / 2^(N+l)) =
+// mulhi_W(2n, m) >> l, so one form covers every divisor.  The push only divides a renormalised
+// state, which is < freq * 2^(state_bits-1-fp) <= 2^N, so the precondition n < 2^N holds.
 #pragma once
 
 #include <cstdint>
@@ -31,6 +31,7 @@ enum : uint32_t {
   DEV_UNDERFLOW = 8u,
   DEV_BAD_FREQ = 16u,
   DEV_BAD_ESCAPE = 32u,
+  DEV_STALLED = 64u,  // a bounded wait between the warps of a block ran out; the rows are not valid
 };
 
 template <int V> struct Variant;
@@ -70,15 +71,20 @@ template <typename S> __device__ __forceinline__ S to_state(int32_t a) {
 }
 
 // One encode-table entry: everything the push needs about (table k, symbol v), 16 bytes.
-//   x: low 32 bits of the reciprocal, y: high 32 bits (64-bit state only),
-//   z: frequency (0 marks an unusable entry: freq <= 0), w: start = cdf[v] (int32 bits)
-__device__ __forceinline__ unsigned shift_for(uint32_t d) {  // l - 1, l = ceil(log2 d); 0 for d < 2
-  return d > 1u ? 31u - (unsigned)__clz((int)(d - 1u)) : 0u;
+//   x, y: the reciprocal m = ceil(2^(N+l) / freq) (y = high word, 64-bit state only), with
+//         l = ceil(log2 freq) and N = 63 (64-bit state) or 31 (32-bit states);
+//   z:    freq, and when fp <= 23 also l in bits 24..28 (freq < 2^24 then);
+//   w:    start = cdf[v] (int32 bits).
+// z = 0 marks an unusable entry (freq <= 0).  Quotient: floor(x / freq) = mulhi(2x, m) >> l for
+// every freq >= 1 and x < 2^N (the GM bound above, with 2x absorbing the one-bit shift; for
+// freq = 1, l = 0 and m = 2^N give floor(2x * 2^N / 2^(N+1)) = x), so there is no special case.
+__device__ __forceinline__ unsigned ceil_log2(uint32_t d) {  // 0 for d <= 1
+  return d > 1u ? 32u - (unsigned)__clz((int)(d - 1u)) : 0u;
 }
 
 __device__ __forceinline__ unsigned long long recip64(uint32_t d) {
-  // m = ceil(2^(63+l) / d) computed as two 64-bit divisions (2^(63+l) = 2^(31+l) * 2^32)
-  const unsigned l = 32u - (unsigned)__clz((int)(d - 1u));
+  // m = ceil(2^(63+l) / d) as two 64-bit divisions (2^(63+l) = 2^(31+l) * 2^32); d = 1 -> 2^63
+  const unsigned l = ceil_log2(d);
   const unsigned long long A = 1ull << (31 + l);
   const unsigned long long qa = A / d, ra = A % d;
   const unsigned long long hi = ra << 32;
@@ -86,21 +92,24 @@ __device__ __forceinline__ unsigned long long recip64(uint32_t d) {
   return (qa << 32) + qb + (rb != 0 ? 1ull : 0ull);
 }
 
-__device__ __forceinline__ uint32_t recip32(uint32_t d) {
-  const unsigned l = 32u - (unsigned)__clz((int)(d - 1u));
+__device__ __forceinline__ uint32_t recip32(uint32_t d) {  // ceil(2^(31+l) / d); d = 1 -> 2^31
+  const unsigned l = ceil_log2(d);
   const unsigned long long A = 1ull << (31 + l);
   return (uint32_t)((A + d - 1) / d);
 }
 
+// freq and l of an entry (l packed when the caller's fp <= 23)
+__device__ __forceinline__ uint32_t entry_freq(uint4 e, bool packed) { return packed ? (e.z & 0xFFFFFFu) : e.z; }
+__device__ __forceinline__ unsigned entry_shift(uint4 e, bool packed) { return packed ? (e.z >> 24) : ceil_log2(e.z); }
+
 template <int V>
-__device__ __forceinline__ typename VT<V>::State quotient(typename VT<V>::State x, uint4 e) {
+__device__ __forceinline__ typename VT<V>::State quotient(typename VT<V>::State x, uint4 e, bool packed) {
+  const unsigned l = entry_shift(e, packed);
   if constexpr (V == 0) {
     const unsigned long long m = ((unsigned long long)e.y << 32) | e.x;
-    const unsigned long long q = __umul64hi(x, m) >> shift_for(e.z);
-    return e.z == 1u ? x : q;
+    return __umul64hi(x << 1, m) >> l;
   } else {
-    const uint32_t q = __umulhi(x, e.x) >> shift_for(e.z);
-    return e.z == 1u ? x : q;
+    return __umulhi(x << 1, e.x) >> l;
   }
 }
 
@@ -168,6 +177,47 @@ __device__ __forceinline__ void cp_async4(void* smem, const void* gmem) {
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
 template <int N> __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
+
+// ---------------------------------------------------------------- shared-memory barriers
+// mbarrier objects (8 bytes of shared memory each) hand ring slots between the warps of a block.
+// A phase completes when its expected arrivals are in; waiters name the phase by its parity.
+__device__ __forceinline__ unsigned smem_u32(const void* p) { return (unsigned)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ void mbar_init(unsigned long long* b, unsigned count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(smem_u32(b)), "r"(count) : "memory");
+}
+// arrive with release semantics: this thread's earlier shared-memory writes (and reads) are
+// ordered before the phase completes
+__device__ __forceinline__ void mbar_arrive(unsigned long long* b) {
+  asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];\n" ::"r"(smem_u32(b)) : "memory");
+}
+// arrive once every cp.async this thread issued so far has landed (counts as one of the
+// expected arrivals)
+__device__ __forceinline__ void mbar_arrive_cp_async(unsigned long long* b) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];\n" ::"r"(smem_u32(b)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(unsigned long long* b, unsigned parity) {
+  unsigned ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(b)), "r"(parity)
+      : "memory");
+  return ok != 0u;
+}
+// Warp-uniform bounded wait (call with the whole warp converged).  Gives up after `limit` tries
+// (each try_wait may suspend the warp for a short while) or as soon as another warp of the block
+// has given up (*abort != 0); returns whether the phase completed.
+__device__ __forceinline__ bool warp_wait(unsigned long long* b, unsigned parity, volatile int* abort,
+                                          unsigned limit) {
+  for (unsigned it = 0; it < limit; ++it) {
+    const bool done = mbar_try_wait(b, parity);
+    if (__all_sync(0xffffffffu, done)) return true;
+    if (__any_sync(0xffffffffu, *abort != 0)) return false;
+  }
+  return false;
 }
 
 // L2 eviction policies: tables that every step reads stay (evict_last); data read or written

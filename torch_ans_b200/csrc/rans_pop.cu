@@ -20,6 +20,7 @@
 #include "rans_host.h"
 #include "rans_pop.cuh"
 #include "rans_pop_fast.cuh"
+#include "rans_pop_lean.cuh"
 
 namespace tans {
 
@@ -74,12 +75,15 @@ __global__ void build_split_s_kernel(const int32_t* cdfs, int64_t ntables, int64
   }
 }
 
-// Bucket table: one 8-byte entry per 16 consecutive cum values of a table, words
-//   w0 = s0 | two << 15, w1 = start of s0, w2 = (two ? start of s0+1 : freq of s0 mod 2^16),
-//   w3 = (two ? end of s0+1 mod 2^16 : 0)
-// where s0 is the symbol of the bucket's first cum and `two` says one more symbol starts inside
-// the bucket.  Every cum of the bucket is checked against the reference lookup; a bucket the
-// entry cannot reproduce exactly is marked w0 = 0xFFFF and decoded through the split tables.
+// Bucket table: one 8-byte entry per 16 consecutive cum values of a table,
+//   bits  0..15  s0, the symbol of the bucket's first cum (0xFFFF: the entry cannot describe the
+//                bucket; those cum values are decoded through the split tables),
+//   bits 16..31  start0, the start of s0 (it may lie before the bucket),
+//   bits 32..47  freq(s0) - 1,
+//   bits 48..63  freq(s0 + 1) - 1 (0 when s0 covers the whole bucket).
+// Decode: c1 = start0 + freq(s0); a cum below c1 is s0 (start0, freq(s0)), a cum at or past c1 is
+// s0 + 1 (start c1, freq(s0 + 1)), so at most one boundary lies inside a bucket.  Every cum of the
+// bucket is checked against the reference lookup when the entry is built.
 template <int V, int LK>
 __global__ void build_bucket_kernel(const int32_t* cdfs, int64_t ntables, int64_t cdf_width, const TableInfo* tinfo,
                                     int fp, unsigned long long* BK) {
@@ -94,9 +98,10 @@ __global__ void build_bucket_kernel(const int32_t* cdfs, int64_t ntables, int64_
     int32_t off0 = 0, f0 = 0;
     bool good = lookup_symbol<V, LK>(row, t, lo, cdf_width, fp, s0, off0, f0);
     const int32_t start0 = lo - off0;
-    good = good && s0 >= 0 && s0 < 0x7FFF && start0 >= 0 && start0 <= 0xFFFF && f0 >= 1 && f0 <= 0x10000;
-    bool two = false;
-    int32_t c1 = 0, f1 = 0;
+    good = good && s0 >= 0 && s0 < 0xFFFE && start0 >= 0 && start0 <= 0xFFFF && f0 >= 1 && f0 <= 0x10000;
+    const int32_t c1 = start0 + f0;
+    int32_t f1 = 1;
+    bool seen1 = false;
     for (int i = 1; good && i < (1 << kBucketBits); ++i) {
       int64_t s;
       int32_t off, f;
@@ -106,26 +111,19 @@ __global__ void build_bucket_kernel(const int32_t* cdfs, int64_t ntables, int64_
         break;
       }
       const int32_t st = cum - off;
-      if (s == s0) {
-        good = !two && st == start0 && f == f0;
-      } else if (s == s0 + 1 && !two) {
-        two = true;
-        c1 = st;
-        f1 = f;
-        good = c1 == cum && c1 <= 0xFFFF && f1 >= 1 && f1 <= 0x10000;
+      if (cum < c1) {
+        good = s == s0 && st == start0 && f == f0;
       } else {
-        good = two && s == s0 + 1 && st == c1 && f == f1;
+        if (!seen1) {
+          f1 = f;
+          seen1 = true;
+        }
+        good = s == s0 + 1 && st == c1 && f == f1 && f1 >= 1 && f1 <= 0x10000;
       }
     }
-    if (good) {
-      const uint32_t w0 = (uint32_t)s0 | (two ? 0x8000u : 0u);
-      const uint32_t w2 = two ? (uint32_t)c1 : ((uint32_t)f0 & 0xFFFFu);
-      const uint32_t w3 = two ? ((uint32_t)(c1 + f1) & 0xFFFFu) : 0u;
-      // the start..stop difference of the last symbol of a `two` bucket must reproduce f0 too
-      if (!two || ((uint32_t)(c1 - start0) == (uint32_t)f0))
-        out = (unsigned long long)w0 | ((unsigned long long)start0 << 16) | ((unsigned long long)w2 << 32) |
-              ((unsigned long long)w3 << 48);
-    }
+    if (good)
+      out = (unsigned long long)s0 | ((unsigned long long)start0 << 16) | ((unsigned long long)(f0 - 1) << 32) |
+            ((unsigned long long)(f1 - 1) << 48);
     BK[e] = out;
   }
 }
@@ -390,6 +388,7 @@ size_t pop_workspace_bytes(int variant, int lookup, int64_t ntables, int64_t cdf
 
 template <int V, int LK, bool BYPASS>
 static void launch_pop(const PopParams& P, int interleave, const LaunchShape& L, cudaStream_t s) {
+  note_launch();
   if (interleave == 4) {
     pop_i4_kernel<V, LK, BYPASS><<<L.blocks, L.threads, 0, s>>>(P);
     return;
@@ -431,6 +430,7 @@ static void build_tables(const PopParams& P, int lookup, bool fused, uint32_t* D
                          int sms, cudaStream_t s) {
   const int64_t m = P.ntables << P.fp;
   const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>((m + 255) / 256, 8 * (int64_t)sms));
+  note_launch();
   if (fused) {
     if (lookup == TANS_LOOKUP_ALIAS)
       build_fused_kernel<V, LK_ALIAS><<<blocks, 256, 0, s>>>(P.cdfs, P.ntables, P.cdf_width, P.tinfo, P.fp, D, Sx);
@@ -449,6 +449,7 @@ static void build_tables(const PopParams& P, int lookup, bool fused, uint32_t* D
   const int64_t n = P.ntables * P.st_stride;
   const int b2 = (int)std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, 8 * (int64_t)sms));
   build_split_st_kernel<<<b2, 256, 0, s>>>(P.cdfs, P.ntables, P.cdf_width, P.st_stride, ST);
+  note_launch();
 }
 
 // launch shape of the fast kernel: streams spread over all SMs, up to 4 warps per SM, then up to
@@ -473,11 +474,40 @@ static LaunchShape fast_shape(int64_t streams, int sms, int& spt) {
   }
   const int lanes_env = env_int("TORCH_ANS_B200_POP_LANES", 0);
   if (lanes_env > 0 && lanes_env <= 32) lanes = lanes_env;
+  // trim the warp count to the lanes actually needed so that the blocks cover every SM
+  // (55.4 streams per SM as 14 warps x 4 lanes: 147 blocks rather than 128 blocks of 16 x 4)
+  warps = std::max<int64_t>(1, std::min<int64_t>(warps, (threads_sm + lanes - 1) / lanes));
   spt = (int)sp;
   L.lanes = (int)lanes;
   L.threads = (int)(warps * 32);
   L.blocks = (int)((streams + warps * lanes * sp - 1) / (warps * lanes * sp));
   return L;
+}
+
+// launch shape of the lean kernel: one stream per thread, streams spread over every SM
+static LaunchShape lean_shape(int64_t streams, int sms) {
+  LaunchShape L{1, 32, 1};
+  const int64_t per_sm = (streams + sms - 1) / sms;
+  int64_t warps = std::min<int64_t>(per_sm, env_int("TORCH_ANS_B200_POPL_WARPS", 16));
+  warps = std::max<int64_t>(1, std::min<int64_t>(warps, 16));
+  int64_t lanes = std::min<int64_t>(32, (per_sm + warps - 1) / warps);
+  const int lanes_env = env_int("TORCH_ANS_B200_POPL_LANES", 0);
+  if (lanes_env > 0 && lanes_env <= 32) lanes = lanes_env;
+  warps = std::max<int64_t>(1, std::min<int64_t>(16, (per_sm + lanes - 1) / lanes));
+  L.lanes = (int)lanes;
+  L.threads = (int)(warps * 32);
+  L.blocks = (int)((streams + warps * lanes - 1) / (warps * lanes));
+  return L;
+}
+
+// TORCH_ANS_B200_POP_KERNEL: "lean" (default), "fast" (several streams per thread) or "generic"
+static int pop_kernel_choice() {
+  const char* e = std::getenv("TORCH_ANS_B200_POP_KERNEL");
+  if (!e || !*e) return 0;
+  const std::string v(e);
+  if (v == "fast") return 1;
+  if (v == "generic") return 2;
+  return 0;
 }
 
 static int layout_override() {
@@ -514,10 +544,12 @@ int pop_impl(int variant, int lookup, int interleave, int32_t* stream, int64_t b
   LaunchShape L{};
   size_t smem = 0;
   bool tin_smem = false;
-  const int ov = layout_override();
-  if (use_tables && ov != 100 && nsym % 4 == 0 && vec_idx && vec_out) {
-    L = fast_shape(batch, dev_sms, spt);
-    const int64_t ring = (int64_t)(L.threads / 32) * L.lanes * POPF_RS * 16 * spt;
+  const int kchoice = pop_kernel_choice();
+  const int ov = kchoice == 2 ? 100 : layout_override();
+  const bool lean = kchoice == 0;
+  if (use_tables && ov != 100 && nsym % 4 == 0 && vec_idx && vec_out && nsym / 4 < 0x7fffffff) {
+    L = lean ? lean_shape(batch, dev_sms) : fast_shape(batch, dev_sms, spt);
+    const int64_t ring = lean ? 0 : (int64_t)(L.threads / 32) * L.lanes * POPF_RS * 16 * spt;
     tin_smem = true;  // the fast kernel always stages the per-table info
     const int64_t avail = (ntables <= 4096) ? kSmemBudget - ring : -1;
     auto fits = [&](int t) {
@@ -602,6 +634,7 @@ int pop_impl(int variant, int lookup, int interleave, int32_t* stream, int64_t b
   {
     const int blocks = (int)std::min<int64_t>((ntables + 255) / 256, 4 * (int64_t)dev_sms);
     build_table_info_kernel<<<blocks > 0 ? blocks : 1, 256, 0, s>>>(sizes, offsets, ntables, fp, tinfo);
+    note_launch();
   }
   if (need_fused || need_split) {
     uint32_t* D = const_cast<uint32_t*>(P.fD);
@@ -615,6 +648,7 @@ int pop_impl(int variant, int lookup, int interleave, int32_t* stream, int64_t b
     unsigned long long* BK = const_cast<unsigned long long*>(P.fBK);
     const int64_t nbk = ntables << (fp - kBucketBits);
     const int bb = (int)std::max<int64_t>(1, std::min<int64_t>((nbk + 127) / 128, 16 * (int64_t)dev_sms));
+    note_launch();
     if (lookup == TANS_LOOKUP_INVCDF) {
       if (variant == TANS_RANS64) build_bucket_kernel<0, LK_INVCDF><<<bb, 128, 0, s>>>(cdfs, ntables, cdf_width, tinfo, fp, BK);
       else if (variant == TANS_RANS32) build_bucket_kernel<1, LK_INVCDF><<<bb, 128, 0, s>>>(cdfs, ntables, cdf_width, tinfo, fp, BK);
@@ -630,7 +664,11 @@ int pop_impl(int variant, int lookup, int interleave, int32_t* stream, int64_t b
     P.tin_smem = tin_smem ? 1 : 0;
     P.spt = spt;
     bool launched;
-    if (variant == TANS_RANS64) launched = launch_pop_fast<0>(P, lookup, bypass != 0, tm, spt, L.blocks, L.threads, smem, s);
+    if (lean) {
+      if (variant == TANS_RANS64) launched = launch_pop_lean<0>(P, lookup, bypass != 0, tm, L.blocks, L.threads, smem, s);
+      else if (variant == TANS_RANS32) launched = launch_pop_lean<1>(P, lookup, bypass != 0, tm, L.blocks, L.threads, smem, s);
+      else launched = launch_pop_lean<2>(P, lookup, bypass != 0, tm, L.blocks, L.threads, smem, s);
+    } else if (variant == TANS_RANS64) launched = launch_pop_fast<0>(P, lookup, bypass != 0, tm, spt, L.blocks, L.threads, smem, s);
     else if (variant == TANS_RANS32) launched = launch_pop_fast<1>(P, lookup, bypass != 0, tm, spt, L.blocks, L.threads, smem, s);
     else launched = launch_pop_fast<2>(P, lookup, bypass != 0, tm, spt, L.blocks, L.threads, smem, s);
     if (!launched) rc = TANS_E_INVALID_ARGUMENT;

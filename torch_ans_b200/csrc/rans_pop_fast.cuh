@@ -12,9 +12,9 @@
 //   TM_FUSED_SMEM / TM_FUSED_GLOBAL: D[k][cum] = (freq - 1) | (cum - start) << 16, S[k][cum] = s
 //   TM_SPLIT_SMEM / TM_SPLIT_GLOBAL: S[k][cum] = s, ST[k][s] = (freq - 1) | start << 16
 //   TM_BUCKET_GLOBAL: one 8-byte entry per 16 cum values holding the bucket's first symbol, its
-//     start and at most one further boundary, so one load resolves (s, start, freq); buckets the
-//     entry cannot describe (verified per cum at build time) carry a marker and use the split
-//     tables, which are built alongside
+//     start and freq and the freq of the next symbol (so at most one boundary inside the bucket):
+//     one load resolves (s, start, freq); buckets the entry cannot describe (verified per cum at
+//     build time) carry a marker and use the split tables, which are built alongside
 // S = 0xFFFF marks the entries the packed layouts cannot hold; those steps take the direct lookup.
 #pragma once
 
@@ -257,18 +257,15 @@ __global__ void __launch_bounds__(512) pop_fast_kernel(const PopParams P) {
           bool fb_any = false;
 #pragma unroll
           for (int j = 0; j < SPT; ++j) {
-            const uint32_t w0 = (uint32_t)bk[j] & 0xFFFFu, start0 = (uint32_t)(bk[j] >> 16) & 0xFFFFu;
-            const uint32_t c1 = (uint32_t)(bk[j] >> 32) & 0xFFFFu, end1 = (uint32_t)(bk[j] >> 48);
-            fb[j] = w0 == 0xFFFFu;
+            const uint32_t lo = (uint32_t)bk[j], hi = (uint32_t)(bk[j] >> 32);
+            const uint32_t s0 = lo & 0xFFFFu, start0 = lo >> 16;
+            fb[j] = s0 == 0xFFFFu;
             fb_any |= fb[j];
-            const bool two = (w0 >> 15) != 0u;
-            const bool up = two && cum[j] >= c1;
-            const uint32_t s0 = w0 & 0x7FFFu;
+            const uint32_t c1 = start0 + (hi & 0xFFFFu) + 1u;
+            const bool up = cum[j] >= c1;
             sv[j] = s0 + (up ? 1u : 0u);
-            const uint32_t st0 = up ? c1 : start0;
-            const uint32_t stop = two ? (up ? end1 : c1) : (start0 + c1);
-            const uint32_t f = (stop - st0) & 0xFFFFu;
-            d[j] = ((f == 0u ? 0x10000u : f) - 1u) | (st0 << 16);
+            // d = (freq - 1) | start << 16 (start < 2^16 for every describable bucket)
+            d[j] = up ? ((hi >> 16) | (c1 << 16)) : ((hi & 0xFFFFu) | (start0 << 16));
           }
           if (__any_sync(__activemask(), fb_any)) {
 #pragma unroll
@@ -366,6 +363,7 @@ void popf_go(const PopParams& P, int blocks, int threads, size_t smem, cudaStrea
   if (smem > 48 * 1024)
     cudaFuncSetAttribute(pop_fast_kernel<V, LK, BY, TM, SPT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   pop_fast_kernel<V, LK, BY, TM, SPT><<<blocks, threads, smem, s>>>(P);
+  note_launch();
 }
 
 template <int V, int LK, bool BY, int TM>

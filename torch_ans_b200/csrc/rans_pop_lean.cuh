@@ -1,0 +1,267 @@
+// rans_pop_lean.cuh -- single-state pop with the shortest serial step (rows 16-byte aligned,
+// length % 4 == 0).
+//
+// A pop is one serial chain per stream (rans_utils.hpp:379-532 per symbol); with one thread per
+// stream, its speed is the latency of one step.  The step here keeps on that chain only
+//   cum = x mod 2^fp -> table load -> (symbol, start, freq) -> x = freq * (x >> fp) + cum - start
+//   -> refill with the word prefetched into a register,
+// and everything else off it: table indexes arrive as 16-byte loads four chunks ahead, the table row
+// of each step is computed from its index while the previous step's table load is in flight, the
+// symbol's output offset and escape slot come from shared memory, and the four symbols of a chunk
+// leave as one 16-byte store.  Steps the straight-line code cannot do exactly (an index outside the
+// table list, a table entry marked as not describable, an escape, a row whose length points outside
+// it) take the reference-exact step on their own lane; underflow needs no special case (a word
+// outside the row reads as 0 and sets TANS_DEV_UNDERFLOW, as the exact step does).
+//
+// Table layouts are those of the fast kernel (built per call by replaying the reference lookup).
+#pragma once
+
+#include "rans_pop_fast.cuh"
+
+namespace tans {
+
+// state of one stream that the rare exact step reads and writes (passed by value both ways, so the
+// kernel never takes the address of its state or of its parameters and keeps both in registers)
+template <int V> struct LeanState {
+  typename VT<V>::State x, nextw;
+  long long p;
+  uint32_t err;
+  int32_t v;  // decoded symbol (output of the exact step)
+};
+
+// the reference-exact step of one symbol, out of line (rare path); refreshes the prefetched word
+template <int V, int LK, bool BYPASS, int TM>
+__device__ __noinline__ LeanState<V> popl_exact(const PopParams P, LeanState<V> st, const int32_t* row, int32_t k,
+                                                const TableInfo* tsm, const uint32_t* tD, const uint16_t* tS) {
+  FastCursor<V> cur;
+  cur.c.payload = reinterpret_cast<const uint8_t*>(row + 1);
+  cur.c.p = st.p;
+  cur.c.first = VT<V>::SBYTES / VT<V>::WBYTES;
+  cur.c.cap = (P.width - 1) * 4 / VT<V>::WBYTES;
+  cur.c.err = st.err;
+  cur.nextw = st.nextw;
+  typename VT<V>::State x = st.x;
+  st.v = popf_exact<V, LK, BYPASS, TM>(P, x, cur, k, tsm, tD, tS, policy_evict_last());
+  cur.prime();
+  st.x = x;
+  st.nextw = cur.nextw;
+  st.p = cur.c.p;
+  st.err = cur.c.err;
+  return st;
+}
+
+__device__ __forceinline__ int4 ld_idx4(const int32_t* p, unsigned long long policy) {
+  int4 v;
+  asm("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.s32 {%0, %1, %2, %3}, [%4], %5;\n"
+      : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+      : "l"(p), "l"(policy));
+  return v;
+}
+
+template <int V, int LK, bool BYPASS, int TM>
+__global__ void __launch_bounds__(512) pop_lean_kernel(const PopParams P) {
+  using S = typename VT<V>::State;
+  using W = typename VT<V>::Word;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  const int T = blockDim.x, tid = threadIdx.x;
+  const int warps = T >> 5, warp = tid >> 5, lane = tid & 31;
+  TableInfo* tsm = reinterpret_cast<TableInfo*>(smem_raw);
+  int2* tsm2 = reinterpret_cast<int2*>(tsm + P.ntables);  // {offset, escape slot} per table
+  unsigned char* tab = reinterpret_cast<unsigned char*>(tsm2 + P.ntables);
+  const int64_t M = (int64_t)1 << P.fp;
+  const int64_t m = P.ntables << P.fp;
+  uint32_t* tD = reinterpret_cast<uint32_t*>(tab);  // fused: D; split: ST
+  uint16_t* tS = reinterpret_cast<uint16_t*>(
+      tab + (TM == TM_FUSED_SMEM ? m * 4 : (TM == TM_SPLIT_SMEM ? P.ntables * P.st_stride * 4 : 0)));
+  for (int64_t k = tid; k < P.ntables; k += T) {
+    const TableInfo ti = P.tinfo[k];
+    tsm[k] = ti;
+    tsm2[k] = make_int2(ti.offset, BYPASS ? ti.size - 2 : -1);
+  }
+  if constexpr (TM == TM_FUSED_SMEM) {
+    for (int64_t i = tid; i < m; i += T) tD[i] = P.fD[i];
+    for (int64_t i = tid; i < m; i += T) tS[i] = P.fS[i];
+  } else if constexpr (TM == TM_SPLIT_SMEM) {
+    const int64_t n = P.ntables * P.st_stride;
+    for (int64_t i = tid; i < n; i += T) tD[i] = P.fST[i];
+    for (int64_t i = tid; i < m; i += T) tS[i] = P.fS[i];
+  }
+  __syncthreads();
+  if (lane >= P.lanes) return;
+  const int64_t b = ((int64_t)blockIdx.x * warps + warp) * P.lanes + lane;
+  if (b >= P.batch) return;
+
+  int32_t* row = P.stream + b * P.width;
+  FastCursor<V> cur;
+  cur.c.payload = reinterpret_cast<const uint8_t*>(row + 1);
+  cur.c.p = (int64_t)row[0] / VT<V>::WBYTES - 1;
+  cur.c.first = VT<V>::SBYTES / VT<V>::WBYTES;
+  cur.c.cap = (P.width - 1) * 4 / VT<V>::WBYTES;
+  cur.c.err = 0;
+  S x = load_state<V>(row, 0);
+  cur.prime();
+  const W* pw = reinterpret_cast<const W*>(cur.c.payload);
+  // a row whose length points past its end, or past what 32-bit cursors hold, is decoded exactly
+  const bool row_bad = cur.c.p >= cur.c.cap || cur.c.p > 0x7ffffff0;
+  const int first = (int)cur.c.first;
+  const int capw = (int)min(cur.c.cap, (int64_t)0x7fffffff);
+  int p = (int)min(max(cur.c.p, (int64_t)-0x7fffffff), (int64_t)0x7fffffff);
+  S nextw = cur.nextw;
+  uint32_t err = 0;
+
+  const unsigned long long pol_keep = policy_evict_last(), pol_stream = policy_evict_first();
+  const uint32_t cmask = (uint32_t)(M - 1);
+  const uint32_t kmax = (uint32_t)(P.ntables - 1);
+  const int64_t N = P.nsym;
+  const int nch = (int)(N >> 2);
+  const int32_t* irow = P.idx + b * N;
+  // table indexes four chunks (16 steps) ahead of their use: several microseconds even when few
+  // streams share an SM and steps are short
+  int4 kn0 = nch > 0 ? ld_idx4(irow, pol_stream) : make_int4(0, 0, 0, 0);
+  int4 kn1 = nch > 1 ? ld_idx4(irow + 4, pol_stream) : make_int4(0, 0, 0, 0);
+  int4 kn2 = nch > 2 ? ld_idx4(irow + 8, pol_stream) : make_int4(0, 0, 0, 0);
+  int4 kn3 = nch > 3 ? ld_idx4(irow + 12, pol_stream) : make_int4(0, 0, 0, 0);
+
+#pragma unroll 1
+  for (int c = 0; c < nch; ++c) {
+    const int4 k4 = kn0;
+    kn0 = kn1;
+    kn1 = kn2;
+    kn2 = kn3;
+    if (c + 4 < nch) kn3 = ld_idx4(irow + 4 * (int64_t)(c + 4), pol_stream);
+    const int32_t kv[4] = {k4.x, k4.y, k4.z, k4.w};
+    int32_t ov[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int32_t k = kv[q];
+      const uint32_t kc = min((uint32_t)k, kmax);
+      const int2 om = tsm2[kc];
+      const uint32_t cum = (uint32_t)x & cmask;
+      uint32_t sv, fm1, off;
+      bool slow = row_bad || (uint32_t)k > kmax;
+      if constexpr (TM == TM_BUCKET_GLOBAL) {
+        const unsigned long long bk =
+            ld_hint_u64(P.fBK + (((size_t)kc << (P.fp - kBucketBits)) + (cum >> kBucketBits)), pol_keep);
+        const uint32_t lo = (uint32_t)bk, hi = (uint32_t)(bk >> 32);
+        const uint32_t s0 = lo & 0xFFFFu, start0 = lo >> 16;
+        const uint32_t c1 = start0 + (hi & 0xFFFFu) + 1u;
+        const bool up = cum >= c1;
+        slow |= s0 == 0xFFFFu;
+        sv = s0 + (up ? 1u : 0u);
+        fm1 = up ? (hi >> 16) : (hi & 0xFFFFu);
+        off = cum - (up ? c1 : start0);
+      } else if constexpr (TM == TM_FUSED_SMEM || TM == TM_FUSED_GLOBAL) {
+        const size_t e = ((size_t)kc << P.fp) | cum;
+        uint32_t d;
+        if constexpr (TM == TM_FUSED_SMEM) {
+          d = tD[e];
+          sv = tS[e];
+        } else {
+          d = ld_hint_u32(P.fD + e, pol_keep);
+          sv = ld_hint_u16(P.fS + e, pol_keep);
+        }
+        slow |= sv == 0xFFFFu;
+        fm1 = d & 0xFFFFu;
+        off = d >> 16;
+      } else {  // split layouts: S[k][cum], then ST[k][s] = (freq - 1) | start << 16
+        const size_t e = ((size_t)kc << P.fp) | cum;
+        uint32_t st;
+        if constexpr (TM == TM_SPLIT_SMEM) {
+          sv = tS[e];
+          st = tD[(size_t)kc * P.st_stride + min(sv, (uint32_t)(P.st_stride - 1))];
+        } else {
+          sv = ld_hint_u16(P.fS + e, pol_keep);
+          st = ld_hint_u32(P.fST + (size_t)kc * P.st_stride + min(sv, (uint32_t)(P.st_stride - 1)), pol_keep);
+        }
+        slow |= sv == 0xFFFFu;
+        fm1 = st & 0xFFFFu;
+        off = cum - (st >> 16);
+      }
+      if constexpr (BYPASS) slow |= (int32_t)sv == om.y;
+      if (slow) {
+        LeanState<V> st{x, nextw, (long long)p, err, 0};
+        st = popl_exact<V, LK, BYPASS, TM>(P, st, row, k, tsm, tD, tS);
+        x = st.x;
+        nextw = st.nextw;
+        p = (int)min(max(st.p, -0x7fffffffll), 0x7fffffffll);
+        err = st.err;
+        ov[q] = st.v;
+        continue;
+      }
+      x = (S)((x >> P.fp) * (S)(fm1 + 1u) + (S)off);
+      // refill (rans_utils.hpp RANS_POP_STATE_RENORM): the first word is already in a register; a
+      // word outside the row's data reads as 0 and flags underflow, as in the exact step
+      {
+        const bool r = (unsigned long long)x < VT<V>::LB;
+        const int pc = p;
+        if (r && (pc < first || pc >= capw)) err |= DEV_UNDERFLOW;
+        x = r ? (S)((x << VT<V>::WB) | nextw) : x;
+        p = pc - (r ? 1 : 0);
+        if (r) nextw = (p >= first && p < capw) ? (S)__ldg(pw + p) : (S)0;
+      }
+      if constexpr (VT<V>::LOOP) {
+#pragma unroll
+        for (int t = 1; t < VT<V>::MAX_RENORM; ++t) {
+          if ((unsigned long long)x < VT<V>::LB) {
+            if (p < first || p >= capw) err |= DEV_UNDERFLOW;
+            x = (S)((x << VT<V>::WB) | nextw);
+            p -= 1;
+            nextw = (p >= first && p < capw) ? (S)__ldg(pw + p) : (S)0;
+          }
+        }
+      }
+      ov[q] = (int32_t)(sv + (uint32_t)om.x);
+    }
+    int32_t* o = P.out + b * N + 4 * (int64_t)c;
+    st_hint_v4(reinterpret_cast<int4*>(o), make_int4(ov[0], ov[1], ov[2], ov[3]), pol_stream);
+  }
+  store_state<V>(row, 0, x);
+  row[0] = (int32_t)((int64_t)(p + 1) * VT<V>::WBYTES);
+  report(P.status, err);
+}
+
+template <int V>
+bool launch_pop_lean(const PopParams& P, int lookup, bool bypass, int tm, int blocks, int threads, size_t smem,
+                     cudaStream_t s);
+
+template <int V, int LK, bool BY, int TM>
+void popl_go(const PopParams& P, int blocks, int threads, size_t smem, cudaStream_t s) {
+  if (smem > 48 * 1024)
+    cudaFuncSetAttribute(pop_lean_kernel<V, LK, BY, TM>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  pop_lean_kernel<V, LK, BY, TM><<<blocks, threads, smem, s>>>(P);
+  note_launch();
+}
+
+template <int V, bool BY>
+bool popl_tm(const PopParams& P, int lookup, int tm, int blocks, int threads, size_t smem, cudaStream_t s) {
+  if (lookup == 2) {  // alias: only the fused layout (its offsets depend on cum, not on s)
+    if (tm == TM_FUSED_SMEM) popl_go<V, 2, BY, TM_FUSED_SMEM>(P, blocks, threads, smem, s);
+    else if (tm == TM_FUSED_GLOBAL) popl_go<V, 2, BY, TM_FUSED_GLOBAL>(P, blocks, threads, smem, s);
+    else return false;
+    return true;
+  }
+  if (lookup == 1) {
+    if (tm == TM_BUCKET_GLOBAL) popl_go<V, 1, BY, TM_BUCKET_GLOBAL>(P, blocks, threads, smem, s);
+    else if (tm == TM_FUSED_SMEM) popl_go<V, 1, BY, TM_FUSED_SMEM>(P, blocks, threads, smem, s);
+    else if (tm == TM_SPLIT_SMEM) popl_go<V, 1, BY, TM_SPLIT_SMEM>(P, blocks, threads, smem, s);
+    else if (tm == TM_SPLIT_GLOBAL) popl_go<V, 1, BY, TM_SPLIT_GLOBAL>(P, blocks, threads, smem, s);
+    else return false;
+    return true;
+  }
+  if (tm == TM_BUCKET_GLOBAL) popl_go<V, 0, BY, TM_BUCKET_GLOBAL>(P, blocks, threads, smem, s);
+  else if (tm == TM_FUSED_SMEM) popl_go<V, 0, BY, TM_FUSED_SMEM>(P, blocks, threads, smem, s);
+  else if (tm == TM_SPLIT_SMEM) popl_go<V, 0, BY, TM_SPLIT_SMEM>(P, blocks, threads, smem, s);
+  else if (tm == TM_SPLIT_GLOBAL) popl_go<V, 0, BY, TM_SPLIT_GLOBAL>(P, blocks, threads, smem, s);
+  else return false;
+  return true;
+}
+
+#define TANS_DEFINE_POP_LEAN(VV)                                                                               \
+  template <>                                                                                                  \
+  bool launch_pop_lean<VV>(const PopParams& P, int lookup, bool bypass, int tm, int blocks, int threads,       \
+                           size_t smem, cudaStream_t s) {                                                      \
+    return bypass ? popl_tm<VV, true>(P, lookup, tm, blocks, threads, smem, s)                                 \
+                  : popl_tm<VV, false>(P, lookup, tm, blocks, threads, smem, s);                               \
+  }
+
+}  // namespace tans

@@ -15,6 +15,8 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cstdlib>
+#include <string>
 
 #include "../../include/torch_ans_b200.h"
 #include "launch.cuh"
@@ -22,6 +24,7 @@
 #include "rans_host.h"
 #include "rans_push_common.cuh"
 #include "rans_push_fast.cuh"
+#include "rans_push_ws.cuh"
 
 namespace tans {
 
@@ -42,7 +45,7 @@ __global__ void build_table_info_kernel(const int32_t* sizes, const int32_t* off
 
 template <int V>
 __global__ void build_push_entries_kernel(const int32_t* cdfs, int64_t ntables, int64_t cdf_width,
-                                          int64_t stride, uint4* enc) {
+                                          int64_t stride, int fp, uint4* enc) {
   const int64_t total = ntables * stride;
   for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total;
        e += (int64_t)gridDim.x * blockDim.x) {
@@ -52,17 +55,19 @@ __global__ void build_push_entries_kernel(const int32_t* cdfs, int64_t ntables, 
     const int32_t freq = (int32_t)((uint32_t)row[v + 1] - (uint32_t)start);
     uint4 out;
     out.w = (uint32_t)start;
-    if (freq <= 0) {
+    // at fp <= 23 the shift is packed above a 24-bit frequency; a step of 2^24 or more there is
+    // larger than the whole cdf range (no quantised cdf has one) and is reported as a bad frequency
+    if (freq <= 0 || (fp <= 23 && freq >= (1 << 24))) {
       out.x = out.y = out.z = 0u;
     } else {
       const uint32_t d = (uint32_t)freq;
-      out.z = d;
+      out.z = fp <= 23 ? (d | (ceil_log2(d) << 24)) : d;
       if constexpr (V == 0) {
-        const unsigned long long m = d > 1u ? recip64(d) : 0ull;
+        const unsigned long long m = recip64(d);
         out.x = (uint32_t)m;
         out.y = (uint32_t)(m >> 32);
       } else {
-        out.x = d > 1u ? recip32(d) : 0u;
+        out.x = recip32(d);
         out.y = 0u;
       }
     }
@@ -292,6 +297,7 @@ size_t push_workspace_bytes(int variant, int64_t ntables, int64_t enc_stride) {
 
 template <int V, bool ALIAS, bool BYPASS>
 static void launch_push(const PushParams& P, int interleave, const LaunchShape& L, cudaStream_t s) {
+  note_launch();
   if (interleave == 4) {
     push_i4_kernel<V, ALIAS, BYPASS><<<L.blocks, L.threads, 0, s>>>(P);
     return;
@@ -313,6 +319,17 @@ static void launch_push_v(const PushParams& P, bool alias, bool bypass, int inte
     if (bypass) launch_push<V, false, true>(P, interleave, L, s);
     else launch_push<V, false, false>(P, interleave, L, s);
   }
+}
+
+// TORCH_ANS_B200_PUSH_KERNEL: "ws" (warp-specialised, default), "chunk" (single-role fast kernel)
+// or "generic"; each falls through to the next when its preconditions do not hold
+static int push_kernel_choice() {
+  const char* e = std::getenv("TORCH_ANS_B200_PUSH_KERNEL");
+  if (!e || !*e) return 0;
+  const std::string v(e);
+  if (v == "chunk") return 1;
+  if (v == "generic") return 2;
+  return 0;
 }
 
 int64_t push_entry_stride(int64_t cdf_width, int fp) {
@@ -348,12 +365,14 @@ int push_impl(int variant, int use_alias, int interleave, int32_t* stream, int64
     const int64_t n = ntables;
     const int blocks = (int)std::min<int64_t>((n + 255) / 256, 4 * (int64_t)dev_sms);
     build_table_info_kernel<<<blocks > 0 ? blocks : 1, 256, 0, s>>>(sizes, offsets, ntables, fp, tinfo);
+    note_launch();
     const int64_t m = ntables * stride;
     const int eb = (int)std::min<int64_t>((m + 255) / 256, 16 * (int64_t)dev_sms);
     if (m > 0) {
-      if (variant == TANS_RANS64) build_push_entries_kernel<0><<<eb, 256, 0, s>>>(cdfs, ntables, cdf_width, stride, enc);
-      else if (variant == TANS_RANS32) build_push_entries_kernel<1><<<eb, 256, 0, s>>>(cdfs, ntables, cdf_width, stride, enc);
-      else build_push_entries_kernel<2><<<eb, 256, 0, s>>>(cdfs, ntables, cdf_width, stride, enc);
+      if (variant == TANS_RANS64) build_push_entries_kernel<0><<<eb, 256, 0, s>>>(cdfs, ntables, cdf_width, stride, fp, enc);
+      else if (variant == TANS_RANS32) build_push_entries_kernel<1><<<eb, 256, 0, s>>>(cdfs, ntables, cdf_width, stride, fp, enc);
+      else build_push_entries_kernel<2><<<eb, 256, 0, s>>>(cdfs, ntables, cdf_width, stride, fp, enc);
+      note_launch();
     }
   }
   PushParams P;
@@ -373,8 +392,49 @@ int push_impl(int variant, int use_alias, int interleave, int32_t* stream, int64
   P.bp = bp;
   P.status = status;
   P.vec = ((reinterpret_cast<uintptr_t>(symbols) | reinterpret_cast<uintptr_t>(indexes)) & 15u) == 0;
+  const int choice = push_kernel_choice();
+  const bool fast_ok = interleave == 1 && nsym > 0 && nsym % 4 == 0 && P.vec && ntables <= 4096 && fp <= 23 &&
+                       nsym / 4 < 0x7fffffff;
+  // ---- warp-specialised kernel: chain warps fed by prep warps through a shared-memory ring
+  if (fast_ok && choice == 0 && (width - 1) * 4 / ((variant == TANS_RANS64) ? 4 : (variant == TANS_RANS32 ? 1 : 2)) <
+                                     (int64_t)0x7fffff00) {
+    const int64_t M = (int64_t)1 << fp;
+    const int64_t remap = use_alias ? ntables * M : 0;
+    const int64_t budget = 200 * 1024;
+    const bool rsmem = use_alias && pushws_smem_bytes(1, true, ntables, remap) <= budget;
+    const int64_t fixed = pushws_smem_bytes(0, use_alias != 0, ntables, rsmem ? remap : 0);
+    const int64_t per = pushws_stream_bytes(use_alias != 0);
+    const int64_t sb_max = fixed < budget ? (budget - fixed) / per : 0;
+    int64_t sb = (batch + dev_sms - 1) / dev_sms;
+    const int sb_env = env_int("TORCH_ANS_B200_PUSHWS_STREAMS", 0);
+    if (sb_env > 0) sb = sb_env;
+    sb = std::min<int64_t>(sb, std::min<int64_t>(sb_max, 128));
+    if (sb >= 1) {
+      int64_t cw = std::min<int64_t>(env_int("TORCH_ANS_B200_PUSHWS_CHAIN_WARPS", 4), sb);
+      cw = std::max<int64_t>(1, std::min<int64_t>(cw, 8));
+      // whole lanes per chain warp, then only the warps those lanes need
+      const int64_t lanes = std::min<int64_t>(32, (sb + cw - 1) / cw);
+      cw = (sb + lanes - 1) / lanes;
+      int64_t pw = env_int("TORCH_ANS_B200_PUSHWS_PREP_WARPS", 0);
+      if (pw <= 0) pw = std::max<int64_t>(1, std::min<int64_t>(4, (WS_G * sb + 31) / 32));
+      pw = std::min<int64_t>(pw, 8);
+      const int blocks = (int)((batch + sb - 1) / sb);
+      const size_t smem = (size_t)(fixed + sb * per);
+      P.lanes = (int)lanes;
+      bool ok;
+      if (variant == TANS_RANS64)
+        ok = launch_push_ws<0>(P, use_alias != 0, bypass != 0, rsmem, blocks, (int)((cw + pw) * 32), (int)sb, (int)cw, smem, s);
+      else if (variant == TANS_RANS32)
+        ok = launch_push_ws<1>(P, use_alias != 0, bypass != 0, rsmem, blocks, (int)((cw + pw) * 32), (int)sb, (int)cw, smem, s);
+      else
+        ok = launch_push_ws<2>(P, use_alias != 0, bypass != 0, rsmem, blocks, (int)((cw + pw) * 32), (int)sb, (int)cw, smem, s);
+      if (owned) cudaFreeAsync(ws, s);
+      if (!ok) return TANS_E_INVALID_ARGUMENT;
+      return cudaGetLastError() == cudaSuccess ? TANS_OK : TANS_E_CUDA;
+    }
+  }
   // ---- fast kernel: aligned rows, length % 4 == 0, table info in shared memory
-  if (interleave == 1 && nsym > 0 && nsym % 4 == 0 && P.vec && ntables <= 4096 && nsym / 4 < 0x7fffffff) {
+  if (fast_ok && choice <= 1) {
     const int64_t per_sm = (batch + dev_sms - 1) / dev_sms;
     int64_t warps = std::min<int64_t>(per_sm, env_int("TORCH_ANS_B200_PUSH_WARPS", 4));
     if (warps < 1) warps = 1;

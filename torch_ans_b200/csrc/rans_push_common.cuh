@@ -132,7 +132,8 @@ __device__ __forceinline__ void push_chain(const PushParams& P, typename VT<V>::
   if constexpr (BYPASS) {
     if (r.flags & PREP_ESC) push_escape<V>(x, c, r.raw, P.bp);
   }
-  const uint32_t freq = r.e.z;
+  const bool packed = P.fp <= 23;
+  const uint32_t freq = entry_freq(r.e, packed);
   if (freq == 0u) {
     c.err |= DEV_BAD_FREQ;
     return;
@@ -141,7 +142,7 @@ __device__ __forceinline__ void push_chain(const PushParams& P, typename VT<V>::
 #pragma unroll
   for (int t = 0; t < VT<V>::MAX_RENORM; ++t)
     if ((unsigned long long)x >= bound) c.emit(x);
-  const S q = quotient<V>(x, r.e);
+  const S q = quotient<V>(x, r.e, packed);
   const S start = to_state<S>((int32_t)r.e.w);
   if constexpr (ALIAS) {
     const S ri = (S)(x - q * (S)freq + start);

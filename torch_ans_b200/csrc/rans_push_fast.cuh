@@ -1,5 +1,5 @@
 // rans_push_fast.cuh -- the fast single-state push kernel (rows 16-byte aligned, length % 4 == 0,
-// at most 4096 tables).
+// at most 4096 tables, frequency precision <= 23 so entries carry their packed shift).
 //
 // Per thread one stream, walked from its last 4-symbol chunk to its first in time steps:
 //   (1) cp.async the symbol and index chunk PF_L1 + PF_L2 steps ahead of its chain;
@@ -130,14 +130,14 @@ __global__ void __launch_bounds__(512) push_fast_kernel(const PushParams P) {
     }
 #pragma unroll
     for (int q = 3; q >= 0; --q) {
-      const uint32_t freq = e[q].z;
+      const uint32_t freq = entry_freq(e[q], true);
       const unsigned long long bound = (unsigned long long)freq << (VT<V>::USED - P.fp);
 #pragma unroll
       for (int u = 0; u < VT<V>::MAX_RENORM; ++u) {
         const bool r = (unsigned long long)x >= bound;
         if (r) cur.emit(x);
       }
-      const S qt = quotient<V>(x, e[q]);
+      const S qt = quotient<V>(x, e[q], true);
       const S start = to_state<S>((int32_t)e[q].w);
       if constexpr (ALIAS) {
         // the raw ring still holds this chunk's indexes (PF_RS > PF_L1 + PF_L2)
@@ -177,6 +177,7 @@ void pushf_go(const PushParams& P, int blocks, int threads, size_t smem, cudaStr
   if (smem > 48 * 1024)
     cudaFuncSetAttribute(push_fast_kernel<V, A, B, R>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   push_fast_kernel<V, A, B, R><<<blocks, threads, smem, s>>>(P);
+  note_launch();
 }
 
 #define TANS_DEFINE_PUSH_FAST(VV)                                                                             \
