@@ -54,6 +54,7 @@ def parse():
     ap.add_argument("--scale", type=float, default=1.0, help="fraction of the configuration's streams")
     ap.add_argument("--length-scale", type=float, default=1.0, help="fraction of the configuration's stream length")
     ap.add_argument("--e2e-steps", type=int, default=2)
+    ap.add_argument("--e2e-chunk", type=int, default=16384, help="symbols per column chunk of the host pipeline")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="target CPU work of the baseline sample")
@@ -250,7 +251,10 @@ def run_ours(args, ws, rank, local):
 
 
 def run_e2e(args, w, ws, rank, dev, _C, push, pop, init_cpu, push_t, pop_t, kw):
-    """Round trip through the public API from pinned host memory (host wall clock)."""
+    """Round trip through the public host-batch API (torch_ans_b200.host_pipeline.HostStreamCoder):
+    pinned host symbols and indexes in, concatenated bitstream out to pinned host memory, then that
+    bitstream and the indexes back in and the decoded symbols out (host wall clock, max over ranks)."""
+    from torch_ans_b200.host_pipeline import HostStreamCoder
     B, N = w.symbols.shape
     h_sym = torch.empty((B, N), dtype=torch.int32, pin_memory=True)
     h_idx = torch.empty((B, N), dtype=torch.int32, pin_memory=True)
@@ -258,38 +262,22 @@ def run_e2e(args, w, ws, rank, dev, _C, push, pop, init_cpu, push_t, pop_t, kw):
     h_sym.copy_(w.symbols)
     h_idx.copy_(w.indexes)
     torch.cuda.synchronize()
+    coder = HostStreamCoder(w.variant, push_t, pop_t, w.cdfs_sizes, w.offsets, freq_precision=w.fp,
+                            bypass_coding=w.bypass, bypass_precision=w.bp, alias=w.push_cdfs is not None,
+                            lookup=w.lookup, device=dev, chunk_symbols=args.e2e_chunk)
     h2d = d2h = 0
-    pinned = {"buf": torch.empty(0, dtype=torch.uint8)}
 
     def once():
         nonlocal h2d, d2h
-        # encode side
-        sym = h_sym.to(dev, non_blocking=True)
-        idx = h_idx.to(dev, non_blocking=True)
-        st = init_cpu.to(dev, non_blocking=True)
-        push(st, sym, idx, push_t, w.cdfs_sizes, w.offsets, **kw)
-        del sym
-        packed = _C.stream_to_merged_tensor(st, 4, None)
-        del st
+        packed = coder.encode(h_sym, h_idx)
         if ws > 1:  # place this rank's records in the job-wide bitstream
             n_local = torch.tensor([packed.numel()], dtype=torch.int64, device=dev)
             sizes = [torch.zeros_like(n_local) for _ in range(ws)]
             dist.all_gather(sizes, n_local)
-        if pinned["buf"].numel() < packed.numel():
-            pinned["buf"] = torch.empty(int(packed.numel() * 1.05) + (1 << 20), dtype=torch.uint8, pin_memory=True)
-        h_packed = pinned["buf"][: packed.numel()]
-        h_packed.copy_(packed, non_blocking=True)
-        torch.cuda.current_stream().synchronize()
-        del packed
-        # decode side
-        idx = h_idx.to(dev, non_blocking=True)
-        st2 = _C.merged_tensor_to_stream(h_packed, 4, None, str(dev))
-        dec = pop(st2, idx, pop_t, w.cdfs_sizes, w.offsets, **kw)
-        h_out.copy_(dec, non_blocking=True)
-        torch.cuda.current_stream().synchronize()
-        h2d = 2 * B * N * 4 + B * N * 4 + h_packed.numel()
-        d2h = h_packed.numel() + B * N * 4
-        return h_packed.numel()
+        coder.decode(packed, h_idx, out=h_out)
+        h2d = 2 * B * N * 4 + B * N * 4 + packed.numel()
+        d2h = packed.numel() + B * N * 4
+        return packed.numel()
 
     once()  # warm-up (pinned buffer allocation, table prep)
     ok = bool(torch.equal(h_out, h_sym))
@@ -299,13 +287,14 @@ def run_e2e(args, w, ws, rank, dev, _C, push, pop, init_cpu, push_t, pop_t, kw):
         once()
     barrier(ws)
     el = (time.perf_counter() - t) / args.e2e_steps
-    ok = ok and bool(torch.equal(h_out, h_sym))
+    ok = ok and bool(torch.equal(h_out, h_sym)) and coder.device_status() == 0
     el = max_over_ranks(el, ws)
     all_ok = max_over_ranks(0.0 if ok else 1.0, ws) == 0.0
-    del h_sym, h_idx, h_out
+    del h_sym, h_idx, h_out, coder
     return {"value": B * N * ws / el / 1e9, "unit": UNIT, "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
             "ms_per_step": el * 1e3, "ok": all_ok,
-            "path": "pinned host -> _C push -> stream_to_merged_tensor -> host -> merged_tensor_to_stream -> _C pop -> host"}
+            "path": "pinned host -> HostStreamCoder.encode (column chunks: H2D || push) -> bitstream on host -> "
+                    "HostStreamCoder.decode (H2D || pop || D2H) -> pinned host"}
 
 
 # ----------------------------------------------------------------------------- reference CPU

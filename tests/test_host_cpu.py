@@ -161,3 +161,25 @@ def test_workload_tables_are_valid_and_seeded():
     inv = m.pop_cdfs[:, 1025:]
     assert inv.shape[1] == 1 << 16
     assert np.array_equal(inv.numpy(), O.inverse_quantized_cdf(m.cdfs.numpy(), 16))
+
+
+@pytest.mark.parametrize("prefix", [1, 2, 4])
+def test_parse_merged_matches_split_merged_bytes(prefix):
+    """The host walk the pipeline decoder uses finds exactly the records split_merged_bytes finds
+    (empty records, records past the end of the data, and a truncated prefix raising)."""
+    import torch
+    from torch_ans_b200 import _C
+    from torch_ans_b200.utils import merge_bytes, split_merged_bytes
+    rng = np.random.default_rng(prefix)
+    cap = (1 << (8 * prefix)) - 1
+    segs = [bytes(rng.integers(0, 256, int(n), dtype=np.uint8)) for n in rng.integers(0, min(cap, 700), 37)]
+    segs[5] = b""
+    data = merge_bytes(segs, num_bytes_length=prefix)
+    t = torch.frombuffer(bytearray(data), dtype=torch.uint8)
+    off, ln = _C.parse_merged(t, prefix, len(segs) + 3)
+    want = split_merged_bytes(data, num_bytes_length=prefix)
+    got = [data[o:o + n] for o, n in zip(off.tolist(), ln.tolist())]
+    assert got[: len(want)] == want and all(g == b"" for g in got[len(want):])
+    if prefix > 1:  # a data tail shorter than one prefix
+        with pytest.raises(RuntimeError, match="truncated"):
+            _C.parse_merged(torch.frombuffer(bytearray(b"\x01" * (prefix - 1)), dtype=torch.uint8), prefix, 1)

@@ -12,7 +12,9 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
+#include <algorithm>
 #include <cstdlib>
+#include <tuple>
 #include <mutex>
 #include <optional>
 #include <string>
@@ -389,6 +391,65 @@ Tensor merged_tensor_to_stream(const Tensor& data, int64_t num_bytes_length, std
   return stream;
 }
 
+// Asynchronous copy of a block of columns between two row-major 2-D tensors with the same number
+// of rows (host <-> device or device <-> device): one pitched copy (cudaMemcpy2DAsync) on the given
+// CUDA stream, so a column range of a pinned host matrix moves without a staging copy on the host.
+void copy_columns(Tensor dst, int64_t dst_col, const Tensor& src, int64_t src_col, int64_t ncols,
+                  int64_t cuda_stream) {
+  TORCH_CHECK(dst.dim() == 2 && src.dim() == 2 && dst.size(0) == src.size(0), "copy_columns: 2-D tensors with equal rows");
+  TORCH_CHECK(dst.scalar_type() == src.scalar_type(), "copy_columns: dtypes differ");
+  TORCH_CHECK(dst.stride(1) == 1 && src.stride(1) == 1, "copy_columns: rows must be contiguous");
+  TORCH_CHECK(ncols >= 0 && dst_col >= 0 && src_col >= 0 && dst_col + ncols <= dst.size(1) &&
+                  src_col + ncols <= src.size(1),
+              "copy_columns: column range outside a tensor");
+  TORCH_CHECK(dst.is_cuda() || dst.is_pinned(), "copy_columns: host side must be pinned");
+  TORCH_CHECK(src.is_cuda() || src.is_pinned(), "copy_columns: host side must be pinned");
+  const int64_t es = (int64_t)src.element_size(), rows = src.size(0);
+  if (rows == 0 || ncols == 0) return;
+  char* d = reinterpret_cast<char*>(dst.data_ptr()) + dst_col * es;
+  const char* s = reinterpret_cast<const char*>(src.data_ptr()) + src_col * es;
+  const cudaError_t e = cudaMemcpy2DAsync(d, (size_t)(dst.stride(0) * es), s, (size_t)(src.stride(0) * es),
+                                          (size_t)(ncols * es), (size_t)rows, cudaMemcpyDefault,
+                                          reinterpret_cast<cudaStream_t>(cuda_stream));
+  TORCH_CHECK(e == cudaSuccess, "copy_columns: ", cudaGetErrorString(e));
+}
+
+// Host walk over a concatenated bitstream (split_merged_bytes semantics, torch_ans/utils.py:74-101):
+// for each of `num_rows` records, the offset of its payload and its length.  Records past the end
+// of the data are empty; a truncated length prefix raises.
+std::tuple<Tensor, Tensor> parse_merged(const Tensor& data, int64_t num_bytes_length, int64_t num_rows) {
+  TORCH_CHECK(!data.is_cuda() && data.scalar_type() == torch::kUInt8 && data.dim() == 1,
+              "data must be a 1-D uint8 CPU tensor");
+  TORCH_CHECK(num_bytes_length == 1 || num_bytes_length == 2 || num_bytes_length == 4,
+              "num_bytes_length must be 1, 2 or 4");
+  TORCH_CHECK(num_rows >= 0, "num_rows must be >= 0");
+  const Tensor dc = data.contiguous();
+  const uint8_t* p = dc.data_ptr<uint8_t>();
+  const int64_t n = dc.numel();
+  Tensor off = torch::empty({num_rows}, torch::TensorOptions().dtype(torch::kInt64));
+  Tensor len = torch::empty({num_rows}, torch::TensorOptions().dtype(torch::kInt32));
+  int64_t* o = off.data_ptr<int64_t>();
+  int32_t* l = len.data_ptr<int32_t>();
+  int64_t pos = 0;
+  for (int64_t r = 0; r < num_rows; ++r) {
+    if (pos >= n) {
+      o[r] = n;
+      l[r] = 0;
+      continue;
+    }
+    TORCH_CHECK(pos + num_bytes_length <= n, "truncated length prefix");
+    uint64_t v = 0;
+    for (int64_t j = 0; j < num_bytes_length; ++j) v |= (uint64_t)p[pos + j] << (8 * j);
+    pos += num_bytes_length;
+    const int64_t take = std::min<int64_t>((int64_t)v, n - pos);
+    TORCH_CHECK(take <= 0x7fffffff, "record longer than 2^31 bytes");
+    o[r] = pos;
+    l[r] = (int32_t)take;
+    pos += take;
+  }
+  return {off, len};
+}
+
 // rans_pmf_to_quantized_cdf (torch_ans/rans_cpu.cpp:326-385) computed on the GPU with the same
 // float32 / int32 tensor arithmetic, then the zero-frequency repair kernel; a CPU input is
 // computed on the current CUDA device and returned on the CPU.
@@ -582,4 +643,9 @@ PYBIND11_MODULE(_C, m) {
   m.def("library_version", []() { return tans_version(); });
   m.def("launch_count", []() { return (uint64_t)tans_launch_count(); },
         "kernels launched by the library in this process so far");
+  m.def("copy_columns", &copy_columns, py::arg("dst"), py::arg("dst_col"), py::arg("src"), py::arg("src_col"),
+        py::arg("ncols"), py::arg("cuda_stream"),
+        "Pitched asynchronous copy of a column block between 2-D tensors (pinned host and/or device).");
+  m.def("parse_merged", &parse_merged, py::arg("data"), py::arg("num_bytes_length"), py::arg("num_rows"),
+        "Payload offsets (int64) and lengths (int32) of the records of a concatenated bitstream.");
 }
