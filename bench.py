@@ -297,6 +297,160 @@ def run_e2e(args, w, ws, rank, dev, _C, push, pop, init_cpu, push_t, pop_t, kw):
                     "HostStreamCoder.decode (H2D || pop || D2H) -> pinned host"}
 
 
+# ----------------------------------------------------------------------------- ragged workload
+def run_ours_ragged(args, ws, rank, local):
+    """Configuration 5: streams of different lengths, one cdf row per symbol (ragged ops)."""
+    from torch_ans_b200 import _C
+    from torch_ans_b200.workloads import ragged_adaptive
+    dev = torch.device("cuda", local)
+    w = ragged_adaptive(dev, scale=args.scale, length_scale=args.length_scale, seed=4 + 1000 * rank)
+    B, T = w.num_streams, w.num_symbols
+    push = getattr(_C, f"{w.variant}_push_ragged")
+    pop = getattr(_C, f"{w.variant}_pop_ragged")
+    kw = dict(freq_precision=w.fp, bypass_coding=w.bypass, bypass_precision=w.bp)
+    init_cpu = getattr(_C, f"{w.variant}_init_stream")(B)
+    lengths = (w.row_starts[1:] - w.row_starts[:-1]).cpu()
+
+    def step(ev=None):
+        st = init_cpu.to(dev, non_blocking=True)
+        if ev:
+            ev[0].record()
+        push(st, w.symbols, w.row_starts, w.cdfs, w.cdfs_sizes, offsets=w.offsets, **kw)
+        if ev:
+            ev[1].record()
+        comp = st[:, 0].clone()
+        dec = pop(st, w.row_starts, w.cdfs, w.cdfs_sizes, offsets=w.offsets, **kw)
+        if ev:
+            ev[2].record()
+        return dec, comp
+
+    for _ in range(args.warmup):
+        dec, comp = step()
+    torch.cuda.synchronize()
+    ok = bool(torch.equal(dec, w.symbols))
+    comp_bytes = float((comp.to(torch.int64) - 4).sum().item())
+    del dec
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        barrier(ws)
+        n_launch0 = _C.launch_count()
+        t0.record()
+        for k in range(args.steps):
+            dec, comp = step(evs[k])
+        t1.record()
+        n_launch = _C.launch_count() - n_launch0
+        barrier(ws)
+    ok = ok and bool(torch.equal(dec, w.symbols)) and _C.device_status() == 0
+    del dec
+    ms = t0.elapsed_time(t1) / args.steps
+    push_ms = sum(e[0].elapsed_time(e[1]) for e in evs) / args.steps
+    pop_ms = sum(e[1].elapsed_time(e[2]) for e in evs) / args.steps
+    ms_max = max_over_ranks(ms, ws)
+    push_ms_max, pop_ms_max = max_over_ranks(push_ms, ws), max_over_ranks(pop_ms, ws)
+    all_ok = max_over_ranks(0.0 if ok else 1.0, ws) == 0.0
+    total = T * ws
+    c = comp_bytes / T
+    # algorithmic bytes: encode reads symbol + the two cdf entries bracketing it and writes c;
+    # decode reads the whole 33-entry row (the symbol is unknown before the lookup), reads c and
+    # writes the symbol
+    A1 = w.cdfs.shape[1]
+    alg = {"push": T * (4 + 8 + c), "pop": T * (4 * A1 + c + 4)}
+    dom = "pop" if pop_ms >= push_ms else "push"
+    dom_ms = pop_ms if dom == "pop" else push_ms
+    peak, peak_kind = measured_peak_hbm()
+    achieved = alg[dom] / (dom_ms / 1e3) / 1e9
+    res = dict(value=total / (ms_max / 1e3) / 1e9, ms=ms_max, gpu_launches=int(n_launch), push_ms=push_ms_max,
+               pop_ms=pop_ms_max, ok=all_ok, nsym=T, B=B, N=int(lengths.max()), comp_bytes_per_symbol=c,
+               clocks=clk.summary(),
+               roofline={"bound": "hbm", "kernel": f"{w.variant}_{dom}_ragged", "achieved": achieved, "peak": peak,
+                         "unit": "GB/s", "frac": achieved / peak, "peak_kind": peak_kind, "traffic": None,
+                         "algorithmic_bytes_per_launch": alg[dom], "launch_ms": dom_ms},
+               encode_gsym_s=total / (push_ms_max / 1e3) / 1e9, decode_gsym_s=total / (pop_ms_max / 1e3) / 1e9,
+               lengths={"total_symbols": T, "max": int(lengths.max()), "mean": float(lengths.double().mean())})
+    del w
+    torch.cuda.empty_cache()
+    return res
+
+
+_RAGGED_REF = None
+
+
+def _ragged_ref_init():
+    global _RAGGED_REF
+    torch.set_num_threads(1)
+    from oracle import build_ref
+    _RAGGED_REF = build_ref.load()
+
+
+def _ragged_ref_worker(task):
+    """One worker's share of the ragged sample: build its streams (same generator recipe), then
+    run the reference op per stream (B = 1), as the reference must for ragged streams."""
+    lengths, seed = task
+    from torch_ans_b200.workloads import quantize_pmf
+    ref = _RAGGED_REF
+    g = torch.Generator().manual_seed(seed)
+    streams = []
+    for n in lengths:
+        p = torch.softmax(torch.randn((n, 32), generator=g, dtype=torch.float64) * 2.0, -1)
+        cdf = quantize_pmf(p, 16)
+        u = torch.randint(0, 1 << 16, (n, 1), generator=g, dtype=torch.int64)
+        sym = (torch.searchsorted(cdf, u, right=True) - 1).reshape(1, n).to(torch.int32)
+        streams.append((sym, cdf.to(torch.int32).contiguous(), torch.full((n,), 33, dtype=torch.int32),
+                        torch.zeros(n, dtype=torch.int32), torch.arange(n, dtype=torch.int32).reshape(1, n)))
+    kw = dict(freq_precision=16, bypass_coding=False, bypass_precision=4)
+    ok = True
+    t0 = time.perf_counter()
+    tp = 0.0
+    for sym, cdf, sizes, offs, idx in streams:
+        st = ref.rans32_init_stream(1)
+        a = time.perf_counter()
+        ref.rans32_push(st, sym, idx, cdf, sizes, offs, **kw)
+        tp += time.perf_counter() - a
+        dec = ref.rans32_pop(st, idx, cdf, sizes, offs, **kw)
+        ok = ok and bool(torch.equal(dec, sym))
+    return sum(lengths), time.perf_counter() - t0, tp, ok
+
+
+def cpu_reference_ragged(seconds, scale, length_scale):
+    """Reference CPU on a bounded sample of the ragged workload: the first streams of the length
+    list (same distribution) up to about `seconds` of work, spread over all host cores as
+    separate processes (the reference op on B = 1 runs on one thread), timed as the slowest
+    worker's push + pop loop."""
+    import multiprocessing as mp
+    from oracle import build_ref
+    from torch_ans_b200.workloads import ragged_lengths
+    if build_ref.load() is None:
+        return None
+    threads = len(os.sched_getaffinity(0))
+    lengths = ragged_lengths(max(1, int(4096 * scale)), length_scale, 4).tolist()
+    budget = int(seconds * threads * 4e6)  # symbols: ~4 M per core-second of push + pop
+    picked, tot = [], 0
+    for n in lengths:
+        if tot + n > budget and picked:
+            break
+        picked.append(int(n))
+        tot += n
+    shares = [[] for _ in range(threads)]
+    loads = [0] * threads
+    for n in sorted(picked, reverse=True):  # longest first onto the least loaded worker
+        j = loads.index(min(loads))
+        shares[j].append(n)
+        loads[j] += n
+    tasks = [(s, 100 + j) for j, s in enumerate(shares) if s]
+    with mp.get_context("spawn").Pool(len(tasks), initializer=_ragged_ref_init) as pool:
+        out = pool.map(_ragged_ref_worker, tasks)
+    nsym = sum(o[0] for o in out)
+    wall = max(o[1] for o in out)
+    tp = max(o[2] for o in out)
+    assert all(o[3] for o in out), "reference CPU round trip failed"
+    return {"value": nsym / wall / 1e9, "unit": UNIT, "cores": len(tasks), "kind": "reference",
+            "sample": f"{len(picked)} of {len(lengths)} streams ({nsym} symbols) of ragged_adaptive, per-stream "
+                      f"B=1 reference calls in {len(tasks)} processes, push + pop",
+            "encode_gsym_s": nsym / tp / 1e9, "decode_gsym_s": nsym / max(wall - tp, 1e-9) / 1e9,
+            "ms_per_step": wall * 1e3}
+
+
 # ----------------------------------------------------------------------------- reference CPU
 def cpu_reference(workload_name, seconds, scale, length_scale, steps=1, warmup=0):
     """Time the reference CPU implementation (oracle/_ref, else the oracle's C port) on a
@@ -370,11 +524,21 @@ def main():
     ws, rank, local = dist_setup()
     cfg = {"workload": args.workload, "scale": args.scale, "length_scale": args.length_scale,
            "l2": "inputs larger than L2 (no flush)", "parallelism": f"stream shards x{ws}" if ws > 1 else "single GPU"}
+    ragged = args.workload == "ragged_adaptive"
     if args.impl == "reference":
         if rank == 0:
             per_step = max(2.0, 150.0 / max(1, args.steps + args.warmup))
-            base = cpu_reference(args.workload, per_step, args.scale, args.length_scale, steps=args.steps,
-                                 warmup=args.warmup)
+            if ragged:
+                base = cpu_reference_ragged(per_step * 4, args.scale, args.length_scale)
+            else:
+                base = cpu_reference(args.workload, per_step, args.scale, args.length_scale, steps=args.steps,
+                                     warmup=args.warmup)
+            if base is None:
+                print(json.dumps({"impl": "reference", "unavailable": "the reference CPU library (oracle/_ref) is "
+                                  "not built on this machine"}), flush=True)
+                if ws > 1:
+                    dist.destroy_process_group()
+                return
             line = {"metric": METRIC, "value": base["value"], "unit": UNIT, "n_gpus": ws, "steps": args.steps,
                     "warmup": args.warmup, "ms_per_step": base["ms_per_step"], "higher_is_better": True, "scaling": "weak",
                     "vs_baseline": None, "dtype": "int64", "data": "synthetic", "config": cfg, "impl": "reference",
@@ -385,11 +549,16 @@ def main():
             dist.destroy_process_group()
         return
 
-    res = run_ours(args, ws, rank, local)
+    res = run_ours_ragged(args, ws, rank, local) if ragged else run_ours(args, ws, rank, local)
     base = None
     if rank == 0 and ws == 1 and not args.no_cpu:
-        base = cpu_reference(args.workload, args.cpu_seconds, args.scale, args.length_scale)
+        if ragged:
+            base = cpu_reference_ragged(args.cpu_seconds, args.scale, args.length_scale)
+        else:
+            base = cpu_reference(args.workload, args.cpu_seconds, args.scale, args.length_scale)
     if rank == 0:
+        if "lengths" in res:
+            cfg["ragged_lengths"] = res["lengths"]
         cfg.update({"streams_per_gpu": res["B"], "symbols_per_stream": res["N"], "global_batch_streams": res["B"] * ws,
                     "compressed_bytes_per_symbol": round(res["comp_bytes_per_symbol"], 4)})
         line = {"metric": METRIC, "value": res["value"], "unit": UNIT, "n_gpus": ws, "steps": args.steps,

@@ -131,6 +131,30 @@ int tans_pop(int variant, int lookup, int num_interleaves,
              int freq_precision, int bypass_coding, int bypass_precision,
              void* workspace, size_t workspace_bytes, uint32_t* dev_status, void* cuda_stream);
 
+/* Ragged coding.  No single reference function corresponds: the reference codes rectangular
+ * (batch, N) tensors only, so streams of different lengths -- typically with one table row per
+ * symbol, the per-element pattern of TorchANSInterface.encode_with_freqs (torch_ans/utils.py:
+ * 704-760) -- take one rans_push / rans_pop call per stream (B = 1, indexes arange(n_b), tables =
+ * that stream's rows).  Here stream row b codes symbols [row_starts[b], row_starts[b+1]) of the
+ * flat arrays, symbol i with table indexes[i] (indexes NULL: table i), and ends up with exactly
+ * the bytes of that per-stream call (rans_push_indexed_cpu / rans_pop_indexed_cpu,
+ * torch_ans/rans_cpu.cpp:44-322, single state).  row_starts: device int64[batch + 1]; a row whose
+ * range is invalid is skipped and flags TANS_DEV_BAD_VALUE.  Pop uses the bisection lookup only.
+ *   workspace: tans_push_ragged_workspace_size(total_symbols) bytes, or NULL to allocate it
+ *   stream-ordered. */
+size_t tans_push_ragged_workspace_size(int64_t total_symbols);
+int tans_push_ragged(int variant, int32_t* stream, int64_t batch, int64_t stream_width,
+                     const int32_t* symbols, const int32_t* indexes, const int64_t* row_starts,
+                     int64_t total_symbols, const int32_t* cdfs, int64_t num_tables, int64_t cdf_width,
+                     const int32_t* cdf_sizes, const int32_t* offsets, int freq_precision, int bypass_coding,
+                     int bypass_precision, void* workspace, size_t workspace_bytes, uint32_t* dev_status,
+                     void* cuda_stream);
+int tans_pop_ragged(int variant, int32_t* stream, int64_t batch, int64_t stream_width, int32_t* out_symbols,
+                    const int32_t* indexes, const int64_t* row_starts, int64_t total_symbols,
+                    const int32_t* cdfs, int64_t num_tables, int64_t cdf_width, const int32_t* cdf_sizes,
+                    const int32_t* offsets, int freq_precision, int bypass_coding, int bypass_precision,
+                    uint32_t* dev_status, void* cuda_stream);
+
 /* Maximum of column 0 (payload length) over the batch rows, written to *out_max (device int32).
  * The device half of the worst-case resize at torch_ans/rans.hpp:105-107. */
 int tans_stream_max_length(const int32_t* stream, int64_t batch, int64_t stream_width,

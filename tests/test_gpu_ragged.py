@@ -1,0 +1,197 @@
+"""Ragged coding (rans*_push_ragged / rans*_pop_ragged, tans_push_ragged / tans_pop_ragged) against
+the oracle run the way the reference has to run it: one B = 1 call per stream, indexes
+arange(n_b), tables = that stream's own rows (the per-element pattern of encode_with_freqs).
+Rows must hold identical lengths and payload bytes, pops must return identical symbols."""
+import zlib
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as O
+from tests import golden_cases as G
+
+pytestmark = pytest.mark.gpu
+
+VARIANTS = ["rans64", "rans32", "rans32_16"]
+
+
+def _per_element_case(rng, variant, bypass, lengths, A=32):
+    """One quantised cdf row per symbol (softmax of N(0, 2^2) logits over A symbols)."""
+    fp = 15 if variant == "rans32_16" else 16
+    T = int(sum(lengths))
+    logits = rng.normal(0.0, 2.0, (T, A))
+    p = np.exp(logits - logits.max(1, keepdims=True))
+    if bypass:
+        p = np.concatenate([p, np.full((T, 1), 1e-3 * p.sum(1, keepdims=True).mean())], 1)
+    p /= p.sum(1, keepdims=True)
+    freqs = np.maximum(1, np.floor(p * ((1 << fp) - p.shape[1])).astype(np.int64)) if T else np.zeros((0, p.shape[1]), np.int64)
+    if T:
+        freqs[np.arange(T), freqs.argmax(1)] += (1 << fp) - freqs.sum(1)
+    cdfs = np.concatenate([np.zeros((T, 1), np.int64), np.cumsum(freqs, 1)], 1).astype(np.int32)
+    sizes = np.full(T, cdfs.shape[1], np.int32)
+    offs = rng.integers(-4, 4, T).astype(np.int32)
+    if bypass:
+        sym = rng.integers(-6, A + 6, T).astype(np.int32) + offs
+    else:
+        u = rng.integers(0, 1 << fp, T)
+        sym = (np.array([np.searchsorted(cdfs[i], u[i], side="right") - 1 for i in range(T)], np.int32) + offs)
+    return fp, cdfs, sizes, offs, sym.astype(np.int32)
+
+
+def _oracle_rows(variant, fp, bypass, lengths, sym, cdfs, sizes, offs, idx=None):
+    """Per-stream reference calls; returns (pushed rows, popped rows, decoded flat symbols)."""
+    pushed, popped, dec = [], [], []
+    lo = 0
+    for n in lengths:
+        hi = lo + int(n)
+        init = O.init_stream(variant, 1)
+        if n == 0:
+            pushed.append(init)
+            popped.append(init.copy())
+            lo = hi
+            continue
+        if idx is None:
+            tab, ts, to, ix = cdfs[lo:hi], sizes[lo:hi], offs[lo:hi], np.arange(n, dtype=np.int32)[None]
+        else:
+            tab, ts, to, ix = cdfs, sizes, offs, idx[lo:hi][None]
+        st, err = O.push(variant, init, sym[lo:hi][None], ix, tab, ts, to, fp, bypass, 4)
+        assert err == 0
+        pushed.append(st)
+        st2 = st.copy()
+        d, derr = O.pop(variant, st2, ix, tab, ts, to, fp, bypass, 4)
+        assert derr == 0
+        popped.append(st2)
+        dec.append(d.reshape(-1))
+        lo = hi
+    return pushed, popped, (np.concatenate(dec) if dec else np.zeros(0, np.int32))
+
+
+def _same_row(got_row, want):
+    return got_row[0] == want[0, 0] and G.payload_bytes(got_row[None]) == G.payload_bytes(want)
+
+
+@pytest.mark.parametrize("variant", VARIANTS)
+@pytest.mark.parametrize("bypass", [False, True])
+@pytest.mark.parametrize("pattern", ["per_element", "shared_tables"])
+@pytest.mark.parametrize("kernel", ["warp", "thread"])
+def test_ragged_round_trip_matches_per_stream_reference(variant, bypass, pattern, kernel, monkeypatch):
+    """Pops through the warp-per-stream kernel (rows of <= 64 entries) and through the
+    thread-per-stream kernel."""
+    from torch_ans_b200 import _C
+    monkeypatch.setenv("TORCH_ANS_B200_RAGGED_POP_WARP", "1" if kernel == "warp" else "0")
+    rng = np.random.default_rng(zlib.crc32(f"ragged-{variant}-{bypass}-{pattern}".encode()))
+    lengths = [0, 1, 3, 4, 5, 17, 64, 257, 1000, 2] + list(rng.integers(0, 400, 30))
+    fp, cdfs, sizes, offs, sym = _per_element_case(rng, variant, bypass, lengths)
+    idx = None
+    if pattern == "shared_tables":  # a few shared rows, explicit indexes per symbol
+        K = 7
+        cdfs, sizes, offs = cdfs[:K].copy(), sizes[:K].copy(), offs[:K].copy()
+        idx = rng.integers(0, K, len(sym)).astype(np.int32)
+        if not bypass:  # resample symbols from their table
+            u = rng.integers(0, 1 << fp, len(sym))
+            sym = np.array([np.searchsorted(cdfs[k], x, side="right") - 1 for k, x in zip(idx, u)], np.int32) + offs[idx]
+        else:
+            sym = (rng.integers(-6, cdfs.shape[1] + 4, len(sym)) + offs[idx]).astype(np.int32)
+    pushed, popped, dec_ref = _oracle_rows(variant, fp, bypass, lengths, sym, cdfs, sizes, offs, idx)
+    rows = torch.tensor(np.concatenate([[0], np.cumsum(lengths)]), dtype=torch.int64)
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    B = len(lengths)
+    st = getattr(_C, f"{variant}_init_stream")(B).cuda()
+    kw = dict(freq_precision=fp, bypass_coding=bypass, bypass_precision=4)
+    getattr(_C, f"{variant}_push_ragged")(st, dev(sym), rows.cuda(), dev(cdfs), dev(sizes),
+                                          indexes=None if idx is None else dev(idx), offsets=dev(offs), **kw)
+    assert _C.device_status() == 0
+    got = st.cpu().numpy()
+    for b in range(B):
+        assert _same_row(got[b], pushed[b]), f"stream {b} (length {lengths[b]})"
+    dec = getattr(_C, f"{variant}_pop_ragged")(st, rows, dev(cdfs), dev(sizes),
+                                               indexes=None if idx is None else dev(idx), offsets=dev(offs), **kw)
+    assert _C.device_status() == 0
+    assert np.array_equal(dec.cpu().numpy(), dec_ref) and np.array_equal(dec_ref, sym)
+    got = st.cpu().numpy()
+    for b in range(B):
+        assert _same_row(got[b], popped[b]), f"stream {b} after pop"
+
+
+@pytest.mark.parametrize("variant", VARIANTS)
+def test_ragged_bad_rows_and_indexes_are_flagged(variant):
+    """An index past the table list skips its step with TANS_DEV_BAD_INDEX (as the rectangular ops
+    do); a row whose range lies outside the flat arrays is left untouched with TANS_DEV_BAD_VALUE;
+    the other rows are still coded exactly."""
+    from torch_ans_b200 import _C
+    rng = np.random.default_rng(7)
+    fp, cdfs, sizes, offs, sym = _per_element_case(rng, variant, False, [5, 6, 7])
+    T = len(sym)
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    kw = dict(freq_precision=fp, bypass_coding=False)
+    # bad index in stream 1 (symbol 7): the oracle restatement skips that step the same way
+    idx = np.arange(T, dtype=np.int32)
+    idx[7] = T + 5
+    rows = torch.tensor([0, 5, 11, 18], dtype=torch.int64)
+    st = getattr(_C, f"{variant}_init_stream")(3).cuda()
+    getattr(_C, f"{variant}_push_ragged")(st, dev(sym), rows.cuda(), dev(cdfs), dev(sizes), indexes=dev(idx),
+                                          offsets=dev(offs), **kw)
+    assert _C.device_status() == O.ERR_BAD_INDEX
+    want, err = O.push(variant, O.init_stream(variant, 1), sym[5:11][None], idx[5:11][None], cdfs, sizes, offs, fp,
+                       False)
+    assert err == O.ERR_BAD_INDEX
+    assert _same_row(st.cpu().numpy()[1], want)
+    # invalid ranges: stream 1 runs past the arrays, stream 2 ends before it starts
+    bad = torch.tensor([0, 5, 30, 18], dtype=torch.int64).cuda()
+    st = getattr(_C, f"{variant}_init_stream")(3).cuda()
+    init = st.cpu().numpy().copy()
+    getattr(_C, f"{variant}_push_ragged")(st, dev(sym), bad, dev(cdfs), dev(sizes), offsets=dev(offs), **kw)
+    assert _C.device_status() == O.ERR_BAD_VALUE
+    got = st.cpu().numpy()
+    want0, _ = O.push(variant, O.init_stream(variant, 1), sym[0:5][None], np.arange(5, dtype=np.int32)[None],
+                      cdfs[0:5], sizes[0:5], offs[0:5], fp, False)
+    assert _same_row(got[0], want0)
+    assert np.array_equal(got[1, :init.shape[1]], init[1]) and np.array_equal(got[2, :init.shape[1]], init[2])
+
+
+@pytest.mark.parametrize("variant", VARIANTS)
+@pytest.mark.parametrize("case", ["unsorted_rows", "wide_rows"])
+def test_ragged_pop_unusual_rows(variant, case):
+    """Rows the ballot search must not take (entries out of order: the reference bisection's
+    answer then differs from a count, so the kernel runs the bisection itself), and rows wider than
+    64 entries (the thread-per-stream kernel).  Decoded symbols, rows and error bits must match
+    the oracle's per-stream pops of the same streams."""
+    from torch_ans_b200 import _C
+    rng = np.random.default_rng(zlib.crc32(f"unusual-{variant}-{case}".encode()))
+    lengths = [0, 1, 9, 40, 33, 70, 3]
+    A = 100 if case == "wide_rows" else 32
+    fp, cdfs, sizes, offs, sym = _per_element_case(rng, variant, False, lengths, A=A)
+    pushed, _, _ = _oracle_rows(variant, fp, False, lengths, sym, cdfs, sizes, offs)
+    pop_cdfs = cdfs.copy()
+    if case == "unsorted_rows":  # swap two interior entries of every third row after the push
+        for i in range(0, len(sym), 3):
+            a, b = 5 + i % 7, 20 + i % 9
+            pop_cdfs[i, a], pop_cdfs[i, b] = pop_cdfs[i, b], pop_cdfs[i, a]
+    # oracle pops of each stream with the (possibly unsorted) rows
+    dec_ref, rows_ref, err_ref = [], [], 0
+    lo = 0
+    for b, n in enumerate(lengths):
+        st = pushed[b].copy()
+        if n:
+            d, e = O.pop(variant, st, np.arange(n, dtype=np.int32)[None], pop_cdfs[lo:lo + n], sizes[lo:lo + n],
+                         offs[lo:lo + n], fp, False)
+            dec_ref.append(d.reshape(-1))
+            err_ref |= e
+        rows_ref.append(st)
+        lo += n
+    dec_ref = np.concatenate(dec_ref)
+    Wd = max(r.shape[1] for r in pushed)
+    host = np.zeros((len(lengths), Wd), np.int32)
+    for b, r in enumerate(pushed):
+        host[b, : r.shape[1]] = r[0]
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    st = dev(host)
+    rows = torch.tensor(np.concatenate([[0], np.cumsum(lengths)]), dtype=torch.int64)
+    dec = getattr(_C, f"{variant}_pop_ragged")(st, rows, dev(pop_cdfs), dev(sizes), offsets=dev(offs),
+                                               freq_precision=fp, bypass_coding=False)
+    assert _C.device_status() == err_ref
+    assert np.array_equal(dec.cpu().numpy(), dec_ref)
+    got = st.cpu().numpy()
+    for b in range(len(lengths)):
+        assert _same_row(got[b], rows_ref[b]), f"stream {b}"

@@ -201,6 +201,112 @@ Tensor rans_pop(Tensor stream, std::optional<Tensor> indexes, std::optional<Tens
   return out;
 }
 
+// ---------------------------------------------------------------- ragged ops (beyond the reference surface)
+// Streams of different lengths over flat symbol / index arrays (row_starts: batch + 1 offsets);
+// each row ends with the bytes one reference push / pop of that stream alone (B = 1) produces.
+Tensor row_starts_on(const Tensor& row_starts, const at::Device& dev, int64_t B) {
+  TORCH_CHECK(row_starts.dim() == 1 && row_starts.size(0) == B + 1, "torch_ans_b200: row_starts must be (batch + 1,)");
+  return row_starts.to(dev, torch::kInt64).contiguous();
+}
+
+int64_t row_starts_total(const Tensor& row_starts) {
+  return row_starts.size(0) > 0 ? row_starts[row_starts.size(0) - 1].item<int64_t>() : 0;
+}
+
+// worst-case width per row (the rule of rans.hpp:105-124 applied to each stream's own length)
+void resize_for_ragged_push(Tensor& stream, const Tensor& rows_d, int64_t freq_precision, bool bypass) {
+  const int64_t B = stream.size(0), W = stream.size(1);
+  if (B == 0) return;
+  Tensor n = rows_d.narrow(0, 1, B) - rows_d.narrow(0, 0, B);
+  Tensor safe = stream.select(1, 0).to(torch::kInt64) + (n * freq_precision + 7).div(8, "floor");
+  if (bypass) safe = safe + n * 4;
+  const int64_t need = safe.max().item<int64_t>();
+  const int64_t safe_w = need / (int64_t)sizeof(int32_t) + 1;
+  if (safe_w > W) {
+    Tensor grown = torch::empty({B, safe_w}, stream.options());
+    grown.narrow(1, 0, W).copy_(stream);
+    stream.set_(grown);
+  }
+}
+
+template <int V>
+void rans_push_ragged(Tensor stream, Tensor symbols, Tensor row_starts, Tensor cdfs, Tensor cdfs_sizes,
+                      std::optional<Tensor> indexes, std::optional<Tensor> offsets, int64_t freq_precision, bool bypass_coding,
+                      int64_t bypass_precision) {
+  require_cuda(stream, "stream");
+  TORCH_CHECK(stream.scalar_type() == torch::kInt32 && stream.dim() == 2 && stream.is_contiguous(),
+              "torch_ans_b200: stream must be a contiguous int32 (B, W) tensor");
+  const at::Device dev = stream.device();
+  c10::cuda::CUDAGuard guard(dev);
+  const int64_t B = stream.size(0);
+  Tensor rows = row_starts_on(row_starts, dev, B);
+  Tensor sym = on_device_i32(symbols.reshape({-1}), dev, "symbols");
+  const int64_t T = sym.size(0);
+  Tensor idx;
+  if (indexes.has_value()) {
+    idx = on_device_i32(indexes->reshape({-1}), dev, "indexes");
+    TORCH_CHECK(idx.size(0) == T, "torch_ans_b200: indexes and symbols must have the same length");
+  }
+  Tensor cdf = on_device_i32(cdfs, dev, "cdfs");
+  Tensor sz = on_device_i32(cdfs_sizes, dev, "cdfs_sizes");
+  TORCH_CHECK(cdf.dim() == 2 && sz.size(0) == cdf.size(0), "torch_ans_b200: cdfs (K, W) with one cdfs_size per row");
+  Tensor off;
+  if (offsets.has_value()) {
+    off = on_device_i32(*offsets, dev, "offsets");
+    TORCH_CHECK(off.size(0) == cdf.size(0), "torch_ans_b200: offsets must have one entry per cdf row");
+  }
+  resize_for_ragged_push(stream, rows, freq_precision, bypass_coding);
+  Tensor ws = torch::empty({(int64_t)tans_push_ragged_workspace_size(T) + 256},
+                           torch::TensorOptions().dtype(torch::kUInt8).device(dev));
+  Tensor& st = status_word(dev);
+  const int rc = tans_push_ragged(V, stream.data_ptr<int32_t>(), B, stream.size(1), sym.data_ptr<int32_t>(),
+                                  idx.defined() ? idx.data_ptr<int32_t>() : nullptr, rows.data_ptr<int64_t>(), T,
+                                  cdf.data_ptr<int32_t>(), cdf.size(0), cdf.size(1), sz.data_ptr<int32_t>(),
+                                  off.defined() ? off.data_ptr<int32_t>() : nullptr, (int)freq_precision,
+                                  bypass_coding ? 1 : 0, (int)bypass_precision, ws.data_ptr(), (size_t)ws.numel(),
+                                  reinterpret_cast<uint32_t*>(st.data_ptr<int32_t>()), cur_stream());
+  check_rc(rc, "ragged push");
+  after_op(dev);
+}
+
+template <int V>
+Tensor rans_pop_ragged(Tensor stream, Tensor row_starts, Tensor cdfs, Tensor cdfs_sizes, std::optional<Tensor> indexes,
+                       std::optional<Tensor> offsets, int64_t freq_precision, bool bypass_coding,
+                       int64_t bypass_precision) {
+  require_cuda(stream, "stream");
+  TORCH_CHECK(stream.scalar_type() == torch::kInt32 && stream.dim() == 2 && stream.is_contiguous(),
+              "torch_ans_b200: stream must be a contiguous int32 (B, W) tensor");
+  const at::Device dev = stream.device();
+  c10::cuda::CUDAGuard guard(dev);
+  const int64_t B = stream.size(0);
+  Tensor rows = row_starts_on(row_starts, dev, B);
+  const int64_t T = row_starts.is_cuda() ? row_starts_total(rows) : row_starts_total(row_starts.to(torch::kInt64));
+  Tensor idx;
+  if (indexes.has_value()) {
+    idx = on_device_i32(indexes->reshape({-1}), dev, "indexes");
+    TORCH_CHECK(idx.size(0) >= T, "torch_ans_b200: indexes shorter than row_starts[-1]");
+  }
+  Tensor cdf = on_device_i32(cdfs, dev, "cdfs");
+  Tensor sz = on_device_i32(cdfs_sizes, dev, "cdfs_sizes");
+  TORCH_CHECK(cdf.dim() == 2 && sz.size(0) == cdf.size(0), "torch_ans_b200: cdfs (K, W) with one cdfs_size per row");
+  Tensor off;
+  if (offsets.has_value()) {
+    off = on_device_i32(*offsets, dev, "offsets");
+    TORCH_CHECK(off.size(0) == cdf.size(0), "torch_ans_b200: offsets must have one entry per cdf row");
+  }
+  Tensor out = torch::zeros({T}, torch::TensorOptions().dtype(torch::kInt32).device(dev));
+  Tensor& st = status_word(dev);
+  const int rc = tans_pop_ragged(V, stream.data_ptr<int32_t>(), B, stream.size(1), out.data_ptr<int32_t>(),
+                                 idx.defined() ? idx.data_ptr<int32_t>() : nullptr, rows.data_ptr<int64_t>(), T,
+                                 cdf.data_ptr<int32_t>(), cdf.size(0), cdf.size(1), sz.data_ptr<int32_t>(),
+                                 off.defined() ? off.data_ptr<int32_t>() : nullptr, (int)freq_precision,
+                                 bypass_coding ? 1 : 0, (int)bypass_precision,
+                                 reinterpret_cast<uint32_t*>(st.data_ptr<int32_t>()), cur_stream());
+  check_rc(rc, "ragged pop");
+  after_op(dev);
+  return out;
+}
+
 // rans_stream_to_byte_strings (torch_ans/rans.cpp:5-21).  For a CUDA stream the payloads are
 // packed on the device first, so only payload bytes cross PCIe (not the worst-case row width).
 std::vector<py::bytes> stream_to_byte_strings(const Tensor& stream) {
@@ -643,6 +749,22 @@ PYBIND11_MODULE(_C, m) {
   m.def("library_version", []() { return tans_version(); });
   m.def("launch_count", []() { return (uint64_t)tans_launch_count(); },
         "kernels launched by the library in this process so far");
+#define TANS_RAGGED_PUSH_ARGS                                                                          \
+  py::arg("stream"), py::arg("symbols"), py::arg("row_starts"), py::arg("cdfs"), py::arg("cdfs_sizes"),        \
+      py::arg("indexes") = py::none(), py::arg("offsets") = py::none(), py::arg("freq_precision") = 16,          \
+      py::arg("bypass_coding") = true, py::arg("bypass_precision") = 4
+#define TANS_RAGGED_POP_ARGS                                                                             \
+  py::arg("stream"), py::arg("row_starts"), py::arg("cdfs"), py::arg("cdfs_sizes"), py::arg("indexes") = py::none(), \
+      py::arg("offsets") = py::none(), py::arg("freq_precision") = 16, py::arg("bypass_coding") = true,            \
+      py::arg("bypass_precision") = 4
+  m.def("rans64_push_ragged", &rans_push_ragged<0>, TANS_RAGGED_PUSH_ARGS,
+        "Push streams of different lengths (row b: symbols[row_starts[b]:row_starts[b+1]]); indexes None = one table per symbol.");
+  m.def("rans32_push_ragged", &rans_push_ragged<1>, TANS_RAGGED_PUSH_ARGS);
+  m.def("rans32_16_push_ragged", &rans_push_ragged<2>, TANS_RAGGED_PUSH_ARGS);
+  m.def("rans64_pop_ragged", &rans_pop_ragged<0>, TANS_RAGGED_POP_ARGS,
+        "Pop streams of different lengths; returns the flat int32 symbols (row_starts[-1] of them).");
+  m.def("rans32_pop_ragged", &rans_pop_ragged<1>, TANS_RAGGED_POP_ARGS);
+  m.def("rans32_16_pop_ragged", &rans_pop_ragged<2>, TANS_RAGGED_POP_ARGS);
   m.def("copy_columns", &copy_columns, py::arg("dst"), py::arg("dst_col"), py::arg("src"), py::arg("src_col"),
         py::arg("ncols"), py::arg("cuda_stream"),
         "Pitched asynchronous copy of a column block between 2-D tensors (pinned host and/or device).");

@@ -88,10 +88,16 @@ __device__ __noinline__ int32_t pop_escape(typename VT<V>::State& x, PopCursor<V
 
 enum : int { LK_SEARCH = 0, LK_INVCDF = 1, LK_ALIAS = 2 };
 
+// a table word: read-only global memory (GLOBAL) or a row staged in shared memory
+template <bool GLOBAL> __device__ __forceinline__ int32_t ldrow(const int32_t* p) {
+  if constexpr (GLOBAL) return __ldg(p);
+  else return *p;
+}
+
 // Symbol lookup of rans_utils.hpp:401-449 for one cum value of table row `row`: sets s and the
 // offset cum - start (alias: cum - alias_start) and the symbol's frequency.  Returns false where
 // the reference would index outside the row (then nothing is read out of bounds).
-template <int V, int LK>
+template <int V, int LK, bool GLOBAL = true>
 __device__ __forceinline__ bool lookup_symbol(const int32_t* row, const TableInfo& t, int32_t cum, int64_t cdf_width,
                                               int fp, int64_t& s, int32_t& cum_off, int32_t& freq) {
   using S = typename VT<V>::State;
@@ -103,30 +109,30 @@ __device__ __forceinline__ bool lookup_symbol(const int32_t* row, const TableInf
     const int32_t id = t.cut_log2 >= 0 ? (cum >> t.cut_log2) : (cum / t.cut);
     const int64_t at = (int64_t)size + 4 * (int64_t)id;
     if (at + 3 >= cdf_width) return false;
-    const int32_t cut_cdf = __ldg(row + at);
-    const int32_t other = __ldg(row + at + 1);
-    const int32_t self_off = __ldg(row + at + 2);
-    const int32_t other_off = __ldg(row + at + 3);
+    const int32_t cut_cdf = ldrow<GLOBAL>(row + at);
+    const int32_t other = ldrow<GLOBAL>(row + at + 1);
+    const int32_t self_off = ldrow<GLOBAL>(row + at + 2);
+    const int32_t other_off = ldrow<GLOBAL>(row + at + 3);
     const bool hi = cum >= cut_cdf;
     s = hi ? other : id;
     cum_off -= hi ? other_off : self_off;
   } else if constexpr (LK == LK_INVCDF) {
     if ((int64_t)size + cum >= cdf_width) return false;
-    s = __ldg(row + size + cum);
+    s = ldrow<GLOBAL>(row + size + cum);
   } else {
     // probe (cdf_size * cum) >> fp, then bisection on [0, cdf_size - 1] (rans_utils.hpp:427-448)
     S ix = to_state<S>((int32_t)((uint32_t)size * (uint32_t)cum) >> fp);
     uint32_t low = 0, high = (uint32_t)(size - 1);
     while (high > low) {
       if ((unsigned long long)ix >= (unsigned long long)size) return false;
-      if (cum >= __ldg(row + ix)) low = (uint32_t)ix + 1u;
+      if (cum >= ldrow<GLOBAL>(row + ix)) low = (uint32_t)ix + 1u;
       else high = (uint32_t)ix;
       ix = (S)((low + high) / 2u);
     }
     s = (int64_t)(unsigned long long)(S)(ix - 1);
   }
   if (s < 0 || s >= (int64_t)size - 1) return false;
-  const int32_t lo_c = __ldg(row + s), hi_c = __ldg(row + s + 1);
+  const int32_t lo_c = ldrow<GLOBAL>(row + s), hi_c = ldrow<GLOBAL>(row + s + 1);
   if constexpr (LK != LK_ALIAS) cum_off -= lo_c;
   freq = (int32_t)((uint32_t)hi_c - (uint32_t)lo_c);
   return true;

@@ -1,0 +1,607 @@
+// rans_ragged.cu -- ragged coding: streams of different lengths over one flat symbol array, each
+// symbol with its own table row if wanted (tans_push_ragged / tans_pop_ragged).
+//
+// The reference codes rectangular (batch, N) tensors only; per-element distributions (every
+// symbol its own cdf row, the pattern of TorchANSInterface.encode_with_freqs, utils.py:704-760)
+// over streams of different lengths take one reference call per stream (B = 1, indexes
+// arange(n_b), tables = that stream's rows).  Here stream b codes symbols
+// [row_starts[b], row_starts[b+1]) of the flat array with table indexes[i] (or table i when
+// indexes is NULL), and its row holds exactly the bytes that per-stream call produces.
+//
+// push: a fully parallel prep pass resolves every symbol to its encode entry (reciprocal, freq,
+//   start, escape value, flags) straight from its table row -- per-element tables are used once,
+//   so a per-table entry table would cost more than it saves -- then one thread per stream runs
+//   the serial chain over its entries (last symbol first), prefetched by cp.async.
+// pop: one thread per stream; table indexes are fetched D1 + D2 steps ahead and each step's table
+//   row (with its size and offset) is copied into a per-thread shared-memory ring D2 steps ahead,
+//   so the bisection of rans_utils.hpp:424-450 reads shared memory only.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+
+#include "../../include/torch_ans_b200.h"
+#include "launch.cuh"
+#include "rans_device.cuh"
+#include "rans_host.h"
+#include "rans_pop.cuh"
+#include "rans_push_common.cuh"
+
+namespace tans {
+
+struct RaggedArgs {
+  int32_t* stream;
+  int64_t batch, width;
+  const int32_t* sym;     // push: flat symbols
+  int32_t* out;           // pop: flat decoded symbols
+  const int32_t* idx;     // flat table indexes or nullptr (symbol i uses table i)
+  const int64_t* rows;    // batch + 1 row starts
+  int64_t total;
+  const int32_t* cdfs;
+  int64_t ntables, cdf_width;
+  const int32_t* sizes;
+  const int32_t* offsets;  // or nullptr
+  int fp, bp;
+  uint32_t* status;
+  uint4* ent;  // push workspace: per-symbol entry
+  int2* aux;   // push workspace: per-symbol {escape value, flags}
+};
+
+__device__ __forceinline__ bool ragged_row(const RaggedArgs& R, int64_t b, int64_t& lo, int64_t& hi) {
+  lo = R.rows[b];
+  hi = R.rows[b + 1];
+  return lo >= 0 && hi >= lo && hi <= R.total;
+}
+
+// ---------------------------------------------------------------- push
+// per symbol: the work of push_prepare (rans_utils.hpp:186-215) plus the entry the push builds
+// per table elsewhere (reciprocal of freq, start), from the symbol's own row
+template <int V, bool BYPASS>
+__global__ void ragged_push_prep_kernel(const RaggedArgs R) {
+  uint32_t err = 0;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < R.total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t k = R.idx ? (int64_t)R.idx[i] : i;
+    uint4 e = make_uint4(0, 0, 0, 0);
+    int2 a = make_int2(0, (int)PREP_SKIP);
+    if (k < 0 || k >= R.ntables) {
+      err |= DEV_BAD_INDEX;
+    } else {
+      const int32_t size = R.sizes[k];
+      const int32_t off = R.offsets ? R.offsets[k] : 0;
+      int32_t v = (int32_t)((uint32_t)R.sym[i] - (uint32_t)off);
+      const int32_t maxv = size - 2;
+      uint32_t flags = 0;
+      int32_t raw = 0;
+      if constexpr (BYPASS) {
+        if (v < 0) {
+          raw = -2 * v - 1;
+          v = maxv;
+        } else if (v >= maxv) {
+          raw = 2 * (v - maxv);
+          v = maxv;
+        }
+        if (v == maxv) flags |= PREP_ESC;
+      }
+      if (v < 0 || v >= size - 1 || (int64_t)v + 1 >= R.cdf_width) {
+        err |= DEV_BAD_VALUE;
+      } else {
+        const int32_t* row = R.cdfs + k * R.cdf_width;
+        const int32_t start = row[v];
+        const int32_t freq = (int32_t)((uint32_t)row[v + 1] - (uint32_t)start);
+        e.w = (uint32_t)start;
+        // same entry rule as the per-table builder: freq <= 0 (or too wide to pack at fp <= 23)
+        // leaves z = 0, which the chain reports as a bad frequency
+        if (freq > 0 && !(R.fp <= 23 && freq >= (1 << 24))) {
+          const uint32_t d = (uint32_t)freq;
+          e.z = R.fp <= 23 ? (d | (ceil_log2(d) << 24)) : d;
+          if constexpr (V == 0) {
+            const unsigned long long m = recip64(d);
+            e.x = (uint32_t)m;
+            e.y = (uint32_t)(m >> 32);
+          } else {
+            e.x = recip32(d);
+          }
+        }
+        a = make_int2(raw, (int)flags);
+      }
+    }
+    R.ent[i] = e;
+    R.aux[i] = a;
+  }
+  report(R.status, err);
+}
+
+constexpr int RG_RS = 32;  // push chain: entry ring slots per thread
+constexpr int RG_D = 24;   // push chain: steps between an entry copy and its use
+
+template <int V, bool BYPASS>
+__global__ void __launch_bounds__(256) ragged_push_chain_kernel(const RaggedArgs R, const PushParams P) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  const int T = blockDim.x, tid = threadIdx.x;
+  uint4* ering = reinterpret_cast<uint4*>(smem_raw);
+  int2* aring = reinterpret_cast<int2*>(ering + RG_RS * T);
+  const int64_t b = (int64_t)blockIdx.x * T + tid;
+  if (b >= R.batch) return;
+  int64_t lo, hi;
+  if (!ragged_row(R, b, lo, hi)) {
+    report(R.status, DEV_BAD_VALUE);
+    return;
+  }
+  int32_t* row = R.stream + b * R.width;
+  PushCursor<V> cur;
+  cur.payload = reinterpret_cast<uint8_t*>(row + 1);
+  cur.p = (int64_t)row[0] / VT<V>::WBYTES - 1;
+  cur.cap = (R.width - 1) * 4 / VT<V>::WBYTES;
+  cur.err = 0;
+  typename VT<V>::State x = load_state<V>(row, 0);
+  const int64_t n = hi - lo;
+  for (int64_t t = 0; t < n + RG_D; ++t) {
+    if (t < n) {  // step t codes symbol hi - 1 - t
+      const int64_t i = hi - 1 - t;
+      const int sl = (int)(t & (RG_RS - 1)) * T + tid;
+      cp_async16(ering + sl, R.ent + i, 16);
+      cp_async8(aring + sl, R.aux + i);
+    }
+    cp_async_commit();
+    cp_async_wait<RG_D - 1>();
+    const int64_t tc = t - RG_D;
+    if (tc < 0) continue;
+    const int sl = (int)(tc & (RG_RS - 1)) * T + tid;
+    PushPrep r;
+    r.e = ering[sl];
+    const int2 a = aring[sl];
+    r.raw = a.x;
+    r.flags = (uint32_t)a.y;
+    r.rbase = 0;
+    r.rcap = 0;
+    push_chain<V, false, BYPASS>(P, x, cur, r);
+  }
+  cp_async_wait<0>();
+  store_state<V>(row, 0, x);
+  row[0] = (int32_t)((cur.p + 1) * VT<V>::WBYTES);
+  report(R.status, cur.err);
+}
+
+// ---------------------------------------------------------------- pop
+// cp.async groups complete in order, so one wait depth serves both copies: a row is copied RP_DR
+// steps before its use and an index RP_DI = 2 RP_DR steps before, so the index a row copy needs
+// has landed by the same wait that lands the rows (a short index lead would force young row
+// copies to land early too and cut the row prefetch short)
+constexpr int RP_DR = 12;             // steps between a row copy and its use
+constexpr int RP_DI = 2 * RP_DR;      // steps between an index copy and its use
+constexpr int RP_WAIT = RP_DR - 1;    // groups allowed in flight after each iteration's commit
+constexpr int RP_RI = 32;             // index ring slots (> RP_DI)
+constexpr int RP_RR = 16;             // row ring slots (> RP_DR)
+
+// 16-byte units of shared memory one staged row occupies (the row rounded out to 16-byte bounds)
+inline int64_t ragged_row_units(int64_t cdf_width) { return (cdf_width + 3) / 4 + 1; }
+
+template <int V, bool BYPASS, bool STAGE>
+__global__ void __launch_bounds__(256) ragged_pop_kernel(const RaggedArgs R, const PopParams P, int units) {
+  using S = typename VT<V>::State;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  const int T = blockDim.x, tid = threadIdx.x;
+  int4* rring = reinterpret_cast<int4*>(smem_raw);                                       // [RR][T][units]
+  int32_t* kring = reinterpret_cast<int32_t*>(rring + (STAGE ? (size_t)RP_RR * T * units : 0));  // [RI][T]
+  int2* tring = reinterpret_cast<int2*>(kring + RP_RI * T);                               // [RR][T]
+  const int64_t b = (int64_t)blockIdx.x * T + tid;
+  if (b >= R.batch) return;
+  int64_t lo, hi;
+  if (!ragged_row(R, b, lo, hi)) {
+    report(R.status, DEV_BAD_VALUE);
+    return;
+  }
+  int32_t* row = R.stream + b * R.width;
+  PopCursor<V> cur;
+  cur.payload = reinterpret_cast<const uint8_t*>(row + 1);
+  cur.p = (int64_t)row[0] / VT<V>::WBYTES - 1;
+  cur.first = VT<V>::SBYTES / VT<V>::WBYTES;
+  cur.cap = (R.width - 1) * 4 / VT<V>::WBYTES;
+  cur.err = 0;
+  S x = load_state<V>(row, 0);
+  const int64_t n = hi - lo;
+  const int64_t total_words = R.ntables * R.cdf_width;
+  // table index of step t (staged in the index ring when the caller gave indexes)
+  auto table_of = [&](int64_t t) -> int64_t {
+    return R.idx ? (int64_t)kring[(int)(t & (RP_RI - 1)) * T + tid] : lo + t;
+  };
+  // iteration j: copy the index of step j, copy the row (and size, offset) of step j - (DI - DR),
+  // commit, wait, decode step j - DI
+  for (int64_t j = 0; j < n + RP_DI; ++j) {
+    if (R.idx && j < n) cp_async4(kring + (int)(j & (RP_RI - 1)) * T + tid, R.idx + lo + j);
+    const int64_t tr = j - (RP_DI - RP_DR);
+    if (tr >= 0 && tr < n) {
+      const int64_t k = table_of(tr);
+      const int sl = (int)(tr & (RP_RR - 1));
+      int2* td = tring + sl * T + tid;
+      if (k >= 0 && k < R.ntables) {
+        if constexpr (STAGE) {
+          // the row rounded out to 16-byte bounds; the tail past the table array reads nothing
+          const int64_t e0 = k * R.cdf_width, base = e0 & ~(int64_t)3;
+          const int64_t nu = (e0 + R.cdf_width - base + 3) / 4;
+          int4* dst = rring + ((size_t)sl * T + tid) * units;
+          for (int64_t u = 0; u < nu; ++u) {
+            const int64_t w0 = base + 4 * u;
+            const int64_t avail = total_words - w0;
+            cp_async16(dst + u, R.cdfs + w0, avail >= 4 ? 16 : (int)(avail > 0 ? avail * 4 : 0));
+          }
+        }
+        cp_async4(&td->x, R.sizes + k);
+        if (R.offsets) cp_async4(&td->y, R.offsets + k);
+        else td->y = 0;
+      }
+    }
+    cp_async_commit();
+    cp_async_wait<RP_WAIT>();
+    const int64_t tc = j - RP_DI;
+    if (tc < 0) continue;
+    const int64_t k = table_of(tc);
+    const int64_t i = lo + tc;
+    if (k < 0 || k >= R.ntables) {
+      cur.err |= DEV_BAD_INDEX;
+      R.out[i] = 0;
+      continue;
+    }
+    const int sl = (int)(tc & (RP_RR - 1));
+    const int2 so = tring[sl * T + tid];
+    TableInfo tinf;
+    tinf.size = so.x;
+    tinf.offset = so.y;
+    tinf.cut = 0;
+    tinf.cut_log2 = -1;
+    const int32_t cum = (int32_t)(uint32_t)(x & (S)((1ull << R.fp) - 1ull));
+    int64_t s;
+    int32_t cum_off, freq;
+    bool found;
+    if constexpr (STAGE) {
+      const int64_t e0 = k * R.cdf_width;
+      const int32_t* srow =
+          reinterpret_cast<const int32_t*>(rring + ((size_t)sl * T + tid) * units) + (e0 - (e0 & ~(int64_t)3));
+      found = lookup_symbol<V, LK_SEARCH, false>(srow, tinf, cum, R.cdf_width, R.fp, s, cum_off, freq);
+    } else {
+      found = lookup_symbol<V, LK_SEARCH, true>(R.cdfs + k * R.cdf_width, tinf, cum, R.cdf_width, R.fp, s, cum_off,
+                                                freq);
+    }
+    if (!found) {
+      cur.err |= DEV_BAD_VALUE;
+      R.out[i] = 0;
+      continue;
+    }
+    const int32_t v = pop_finish<V, BYPASS>(P, x, cur, (int32_t)s, cum_off, freq, tinf.size - 2);
+    R.out[i] = (int32_t)((uint32_t)v + (uint32_t)tinf.offset);
+  }
+  cp_async_wait<0>();
+  store_state<V>(row, 0, x);
+  row[0] = (int32_t)((cur.p + 1) * VT<V>::WBYTES);
+  report(R.status, cur.err);
+}
+
+// One warp per stream, for rows of at most 64 entries (the per-element tables: 33 entries).  Lane
+// l stages entries l and l + 32 of each step's row with 4-byte cp.async RW_D steps ahead (each lane
+// reads back only what it copied itself, so no cross-lane ordering is needed); the search is a
+// ballot (size and offset are staged by lane 0 and broadcast): for a row that is non-decreasing with row[0] <= cum < row[size - 1], the reference's
+// bisection (rans_utils.hpp:424-450) ends at the count of entries j < size - 1 with row[j] <= cum,
+// so s = count - 1 and (start, freq) come from two shuffles.  A row failing that test takes the
+// reference bisection itself (on the staged row).  Every lane carries the same state; the decoded
+// symbols of 32 steps leave as one coalesced store.
+constexpr int RW_D = 12;   // steps between a row copy and its use
+constexpr int RW_R = 16;   // row ring slots per warp (> RW_D)
+constexpr int RW_E = 66;   // staged words per slot: 64 entries + size + offset
+
+template <int V, bool BYPASS>
+__global__ void __launch_bounds__(256) ragged_pop_warp_kernel(const RaggedArgs R, const PopParams P) {
+  using S = typename VT<V>::State;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  const int warps = blockDim.x >> 5, wib = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int32_t* ring = reinterpret_cast<int32_t*>(smem_raw) + (size_t)wib * RW_R * RW_E;
+  const int64_t b = (int64_t)blockIdx.x * warps + wib;
+  if (b >= R.batch) return;
+  int64_t lo, hi;
+  if (!ragged_row(R, b, lo, hi)) {
+    if (lane == 0) report(R.status, DEV_BAD_VALUE);
+    return;
+  }
+  int32_t* row = R.stream + b * R.width;
+  PopCursor<V> cur;
+  cur.payload = reinterpret_cast<const uint8_t*>(row + 1);
+  cur.p = (int64_t)row[0] / VT<V>::WBYTES - 1;
+  cur.first = VT<V>::SBYTES / VT<V>::WBYTES;
+  cur.cap = (R.width - 1) * 4 / VT<V>::WBYTES;
+  cur.err = 0;
+  S x = load_state<V>(row, 0);
+  const int64_t n = hi - lo;
+  const int W = (int)R.cdf_width;
+  int32_t kcur = 0;   // table index held by this lane for steps [32 m, 32 m + 32)
+  int32_t outv = 0;   // decoded symbol of step 32 m + lane
+  auto table_at = [&](int64_t t, int32_t kreg) -> int64_t {
+    return R.idx ? (int64_t)__shfl_sync(0xffffffffu, kreg, (int)(t & 31)) : lo + t;
+  };
+  int32_t kahead = (R.idx && lane < n) ? R.idx[lo + lane] : 0;      // indexes of steps [0, 32)
+  int32_t kahead2 = (R.idx && 32 + lane < n) ? R.idx[lo + 32 + lane] : 0;  // steps [32, 64)
+  // iteration j: stage the row of step j, decode step j - RW_D
+  for (int64_t j = 0; j < n + RW_D; ++j) {
+    if ((j & 31) == 0 && j > 0) {  // rotate the index registers every 32 steps
+      kahead = kahead2;
+      kahead2 = (R.idx && j + 32 + lane < n) ? R.idx[lo + j + 32 + lane] : 0;
+    }
+    if (j < n) {
+      const int64_t k = table_at(j, kahead);
+      int32_t* slot = ring + (int)(j & (RW_R - 1)) * RW_E;
+      if (k >= 0 && k < R.ntables) {
+        const int32_t* src = R.cdfs + k * R.cdf_width;
+        if (lane < W) cp_async4(slot + lane, src + lane);
+        if (lane + 32 < W) cp_async4(slot + 32 + lane, src + 32 + lane);
+        if (lane == 0) {
+          cp_async4(slot + 64, R.sizes + k);
+          if (R.offsets) cp_async4(slot + 65, R.offsets + k);
+        }
+      }
+    }
+    cp_async_commit();
+    const int64_t tc = j - RW_D;
+    if (tc < 0) continue;
+    if ((tc & 31) == 0) {
+      if (tc > 0) R.out[lo + tc - 32 + lane] = outv;  // the previous 32 steps: one coalesced store
+      // indexes of steps [tc, tc + 32): the staging side (RW_D < 32 steps ahead) holds them now
+      kcur = kahead;
+    }
+    cp_async_wait<RW_D - 1>();
+    __syncwarp();  // every lane's staged words are visible to the whole warp
+    const int64_t k = table_at(tc, kcur);
+    int32_t v = 0;
+    if (k < 0 || k >= R.ntables) {
+      cur.err |= DEV_BAD_INDEX;
+    } else {
+      const int32_t* slot = ring + (int)(tc & (RW_R - 1)) * RW_E;
+      TableInfo tinf;
+      tinf.size = __shfl_sync(0xffffffffu, lane == 0 ? slot[64] : 0, 0);
+      tinf.offset = R.offsets ? __shfl_sync(0xffffffffu, lane == 0 ? slot[65] : 0, 0) : 0;
+      tinf.cut = 0;
+      tinf.cut_log2 = -1;
+      const int32_t size = tinf.size;
+      const int32_t cum = (int32_t)(uint32_t)(x & (S)((1ull << R.fp) - 1ull));
+      const int32_t c0 = lane < W ? slot[lane] : 0;
+      const int32_t c1 = lane + 32 < W ? slot[32 + lane] : 0;
+      // fast path: 2 <= size <= W, row non-decreasing on [0, size), row[0] <= cum < row[size - 1]
+      const int32_t n0 = __shfl_down_sync(0xffffffffu, c0, 1);
+      const int32_t c1_first = __shfl_sync(0xffffffffu, c1, 0);
+      const int32_t n1 = __shfl_down_sync(0xffffffffu, c1, 1);
+      const int32_t next0 = lane == 31 ? c1_first : n0;
+      const bool mono = (lane + 1 >= size || c0 <= next0) && (lane + 33 >= size || c1 <= n1);
+      const int32_t last = size >= 1 && size <= 64 ? __shfl_sync(0xffffffffu, size - 1 < 32 ? c0 : c1, (size - 1) & 31)
+                                                    : 0;
+      const int32_t first = __shfl_sync(0xffffffffu, c0, 0);
+      const bool fast = size >= 2 && size <= W && __all_sync(0xffffffffu, mono) && first <= cum && cum < last;
+      int64_t s;
+      int32_t cum_off, freq;
+      bool found;
+      if (fast) {
+        const unsigned m0 = __ballot_sync(0xffffffffu, lane < size - 1 && c0 <= cum);
+        const unsigned m1 = __ballot_sync(0xffffffffu, lane + 32 < size - 1 && c1 <= cum);
+        const int cnt = __popc(m0) + __popc(m1);
+        s = cnt - 1;
+        const int32_t st = __shfl_sync(0xffffffffu, s < 32 ? c0 : c1, (int)(s & 31));
+        const int32_t en = __shfl_sync(0xffffffffu, s + 1 < 32 ? c0 : c1, (int)((s + 1) & 31));
+        cum_off = cum - st;
+        freq = (int32_t)((uint32_t)en - (uint32_t)st);
+        found = true;
+      } else {
+        found = lookup_symbol<V, LK_SEARCH, false>(slot, tinf, cum, R.cdf_width, R.fp, s, cum_off, freq);
+      }
+      if (!found) {
+        cur.err |= DEV_BAD_VALUE;
+      } else {
+        const int32_t d = pop_finish<V, BYPASS>(P, x, cur, (int32_t)s, cum_off, freq, size - 2);
+        v = (int32_t)((uint32_t)d + (uint32_t)tinf.offset);
+      }
+    }
+    if ((int)(tc & 31) == lane) outv = v;
+  }
+  // the last group of decoded symbols (full or partial)
+  const int64_t last = n > 0 ? ((n - 1) & ~(int64_t)31) : 0;
+  if (n > 0 && last + lane < n) R.out[lo + last + lane] = outv;
+  cp_async_wait<0>();
+  if (lane == 0) {
+    store_state<V>(row, 0, x);
+    row[0] = (int32_t)((cur.p + 1) * VT<V>::WBYTES);
+    report(R.status, cur.err);
+  }
+}
+
+// ---------------------------------------------------------------- host side
+static int ragged_threads(int64_t batch, int sms, int64_t smem_per_thread, int max_threads) {
+  int64_t t = (batch + sms - 1) / sms;
+  t = ((t + 31) / 32) * 32;
+  t = std::max<int64_t>(32, std::min<int64_t>(t, max_threads));
+  while (t > 32 && t * smem_per_thread > 200 * 1024) t -= 32;
+  return (int)t;
+}
+
+template <int V, bool BY>
+static void ragged_push_launch(const RaggedArgs& R, const PushParams& P, int sms, cudaStream_t s) {
+  const int pb = (int)std::max<int64_t>(1, std::min<int64_t>((R.total + 255) / 256, 16 * (int64_t)sms));
+  if (R.total > 0) {
+    ragged_push_prep_kernel<V, BY><<<pb, 256, 0, s>>>(R);
+    note_launch();
+  }
+  const int T = ragged_threads(R.batch, sms, RG_RS * 24, 256);
+  const size_t smem = (size_t)T * RG_RS * 24;
+  if (smem > 48 * 1024)
+    cudaFuncSetAttribute(ragged_push_chain_kernel<V, BY>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  ragged_push_chain_kernel<V, BY><<<(int)((R.batch + T - 1) / T), T, smem, s>>>(R, P);
+  note_launch();
+}
+
+template <int V, bool BY>
+static void ragged_pop_warp_launch(const RaggedArgs& R, const PopParams& P, int sms, cudaStream_t s) {
+  int64_t warps = (R.batch + sms - 1) / sms;
+  warps = std::max<int64_t>(1, std::min<int64_t>(warps, 8));
+  const size_t smem = (size_t)warps * RW_R * RW_E * sizeof(int32_t);
+  if (smem > 48 * 1024)
+    cudaFuncSetAttribute(ragged_pop_warp_kernel<V, BY>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  ragged_pop_warp_kernel<V, BY><<<(int)((R.batch + warps - 1) / warps), (int)(warps * 32), smem, s>>>(R, P);
+  note_launch();
+}
+
+template <int V, bool BY, bool STAGE>
+static void ragged_pop_launch(const RaggedArgs& R, const PopParams& P, int units, int sms, cudaStream_t s) {
+  const int64_t per = (STAGE ? (int64_t)RP_RR * units * 16 : 0) + RP_RI * 4 + RP_RR * 8;
+  const int T = ragged_threads(R.batch, sms, per, 256);
+  const size_t smem = (size_t)T * per;
+  if (smem > 48 * 1024)
+    cudaFuncSetAttribute(ragged_pop_kernel<V, BY, STAGE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  ragged_pop_kernel<V, BY, STAGE><<<(int)((R.batch + T - 1) / T), T, smem, s>>>(R, P, units);
+  note_launch();
+}
+
+static int check_ragged(int variant, const int32_t* stream, int64_t batch, int64_t width, const int64_t* rows,
+                        int64_t total, const int32_t* cdfs, int64_t ntables, int64_t cdf_width, const int32_t* sizes,
+                        int fp, int bypass, int bp) {
+  if (variant < 0 || variant > 2 || batch < 0 || total < 0 || ntables < 0 || cdf_width < 0)
+    return TANS_E_INVALID_ARGUMENT;
+  if (fp < 1 || fp > max_precision(variant)) return TANS_E_INVALID_ARGUMENT;
+  if (bypass && (bp < 1 || bp > max_precision(variant))) return TANS_E_INVALID_ARGUMENT;
+  if (batch == 0) return TANS_OK;
+  if (!stream || !rows || width < 1 + (int64_t)state_bytes(variant) / 4) return TANS_E_INVALID_ARGUMENT;
+  if (total > 0 && (!cdfs || !sizes || ntables < 1 || cdf_width < 2)) return TANS_E_INVALID_ARGUMENT;
+  return TANS_OK;
+}
+
+}  // namespace tans
+
+extern "C" size_t tans_push_ragged_workspace_size(int64_t total_symbols) {
+  return total_symbols > 0 ? tans::align_up((size_t)total_symbols * 16) + tans::align_up((size_t)total_symbols * 8)
+                           : 0;
+}
+
+extern "C" int tans_push_ragged(int variant, int32_t* stream, int64_t batch, int64_t stream_width,
+                                const int32_t* symbols, const int32_t* indexes, const int64_t* row_starts,
+                                int64_t total_symbols, const int32_t* cdfs, int64_t num_tables, int64_t cdf_width,
+                                const int32_t* cdf_sizes, const int32_t* offsets, int freq_precision,
+                                int bypass_coding, int bypass_precision, void* workspace, size_t workspace_bytes,
+                                uint32_t* dev_status, void* cuda_stream) {
+  using namespace tans;
+  int rc = check_ragged(variant, stream, batch, stream_width, row_starts, total_symbols, cdfs, num_tables, cdf_width,
+                        cdf_sizes, freq_precision, bypass_coding, bypass_precision);
+  if (rc != TANS_OK) return rc;
+  if (batch == 0) return TANS_OK;
+  if (total_symbols > 0 && !symbols) return TANS_E_INVALID_ARGUMENT;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(cuda_stream);
+  const size_t need = tans_push_ragged_workspace_size(total_symbols);
+  void* ws = workspace;
+  bool owned = false;
+  if (need > 0) {
+    if (!ws) {
+      if (cudaMallocAsync(&ws, need, s) != cudaSuccess) return TANS_E_CUDA;
+      owned = true;
+    } else if (workspace_bytes < need) {
+      return TANS_E_WORKSPACE;
+    }
+  }
+  RaggedArgs R{};
+  R.stream = stream;
+  R.batch = batch;
+  R.width = stream_width;
+  R.sym = symbols;
+  R.idx = indexes;
+  R.rows = row_starts;
+  R.total = total_symbols;
+  R.cdfs = cdfs;
+  R.ntables = num_tables;
+  R.cdf_width = cdf_width;
+  R.sizes = cdf_sizes;
+  R.offsets = offsets;
+  R.fp = freq_precision;
+  R.bp = bypass_precision;
+  R.status = dev_status;
+  R.ent = reinterpret_cast<uint4*>(ws);
+  R.aux = reinterpret_cast<int2*>(reinterpret_cast<char*>(ws) + align_up((size_t)std::max<int64_t>(total_symbols, 0) * 16));
+  PushParams P{};
+  P.fp = freq_precision;
+  P.bp = bypass_precision;
+  P.status = dev_status;
+  const int sms = sm_count();
+  const bool by = bypass_coding != 0;
+  if (variant == TANS_RANS64) {
+    if (by) ragged_push_launch<0, true>(R, P, sms, s);
+    else ragged_push_launch<0, false>(R, P, sms, s);
+  } else if (variant == TANS_RANS32) {
+    if (by) ragged_push_launch<1, true>(R, P, sms, s);
+    else ragged_push_launch<1, false>(R, P, sms, s);
+  } else {
+    if (by) ragged_push_launch<2, true>(R, P, sms, s);
+    else ragged_push_launch<2, false>(R, P, sms, s);
+  }
+  if (owned) cudaFreeAsync(ws, s);
+  return cudaGetLastError() == cudaSuccess ? TANS_OK : TANS_E_CUDA;
+}
+
+extern "C" int tans_pop_ragged(int variant, int32_t* stream, int64_t batch, int64_t stream_width,
+                               int32_t* out_symbols, const int32_t* indexes, const int64_t* row_starts,
+                               int64_t total_symbols, const int32_t* cdfs, int64_t num_tables, int64_t cdf_width,
+                               const int32_t* cdf_sizes, const int32_t* offsets, int freq_precision,
+                               int bypass_coding, int bypass_precision, uint32_t* dev_status, void* cuda_stream) {
+  using namespace tans;
+  int rc = check_ragged(variant, stream, batch, stream_width, row_starts, total_symbols, cdfs, num_tables, cdf_width,
+                        cdf_sizes, freq_precision, bypass_coding, bypass_precision);
+  if (rc != TANS_OK) return rc;
+  if (batch == 0) return TANS_OK;
+  if (total_symbols > 0 && !out_symbols) return TANS_E_INVALID_ARGUMENT;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(cuda_stream);
+  RaggedArgs R{};
+  R.stream = stream;
+  R.batch = batch;
+  R.width = stream_width;
+  R.out = out_symbols;
+  R.idx = indexes;
+  R.rows = row_starts;
+  R.total = total_symbols;
+  R.cdfs = cdfs;
+  R.ntables = num_tables;
+  R.cdf_width = cdf_width;
+  R.sizes = cdf_sizes;
+  R.offsets = offsets;
+  R.fp = freq_precision;
+  R.bp = bypass_precision;
+  R.status = dev_status;
+  PopParams P{};
+  P.fp = freq_precision;
+  P.bp = bypass_precision;
+  P.status = dev_status;
+  const int sms = sm_count();
+  const int units = (int)ragged_row_units(cdf_width);
+  const bool by = bypass_coding != 0;
+  // rows of at most 64 entries: one warp per stream, ballot search
+  if (cdf_width <= 64 && env_int("TORCH_ANS_B200_RAGGED_POP_WARP", 1) != 0) {
+    if (variant == TANS_RANS64) {
+      if (by) ragged_pop_warp_launch<0, true>(R, P, sms, s);
+      else ragged_pop_warp_launch<0, false>(R, P, sms, s);
+    } else if (variant == TANS_RANS32) {
+      if (by) ragged_pop_warp_launch<1, true>(R, P, sms, s);
+      else ragged_pop_warp_launch<1, false>(R, P, sms, s);
+    } else {
+      if (by) ragged_pop_warp_launch<2, true>(R, P, sms, s);
+      else ragged_pop_warp_launch<2, false>(R, P, sms, s);
+    }
+    return cudaGetLastError() == cudaSuccess ? TANS_OK : TANS_E_CUDA;
+  }
+  // otherwise one thread per stream; rows are staged in shared memory when the table array is
+  // 16-byte aligned and a row is small
+  const bool stage = ((reinterpret_cast<uintptr_t>(cdfs) & 15u) == 0) && units <= 32;
+#define TANS_RAGGED_POP(VV)                                                     \
+  if (stage) {                                                                  \
+    if (by) ragged_pop_launch<VV, true, true>(R, P, units, sms, s);             \
+    else ragged_pop_launch<VV, false, true>(R, P, units, sms, s);               \
+  } else {                                                                      \
+    if (by) ragged_pop_launch<VV, true, false>(R, P, units, sms, s);            \
+    else ragged_pop_launch<VV, false, false>(R, P, units, sms, s);              \
+  }
+  if (variant == TANS_RANS64) {
+    TANS_RAGGED_POP(0)
+  } else if (variant == TANS_RANS32) {
+    TANS_RAGGED_POP(1)
+  } else {
+    TANS_RAGGED_POP(2)
+  }
+#undef TANS_RAGGED_POP
+  return cudaGetLastError() == cudaSuccess ? TANS_OK : TANS_E_CUDA;
+}

@@ -79,10 +79,10 @@ def quantize_pmf(p: torch.Tensor, fp: int) -> torch.Tensor:
     frac = want - base
     order = torch.argsort(frac, dim=-1, descending=True, stable=True)
     ranks = torch.empty_like(order)
-    ranks.scatter_(-1, order, torch.arange(A).expand_as(order))
+    ranks.scatter_(-1, order, torch.arange(A, device=p.device).expand_as(order))
     base = base + (ranks < rem.unsqueeze(-1)).to(torch.int64)
     freq = base + 1
-    cdf = torch.zeros(p.shape[:-1] + (A + 1,), dtype=torch.int64)
+    cdf = torch.zeros(p.shape[:-1] + (A + 1,), dtype=torch.int64, device=p.device)
     cdf[..., 1:] = torch.cumsum(freq, -1)
     assert bool((cdf[..., -1] == (1 << fp)).all())
     return cdf
@@ -213,9 +213,69 @@ def mixture_invcdf(device="cuda", scale: float = 1.0, length_scale: float = 1.0,
                     torch.zeros(K, dtype=torch.int32, device=device), pop_cdfs=rows.to(device), lookup="invcdf")
 
 
+@dataclass
+class RaggedWorkload:
+    """Streams of different lengths over flat arrays, one cdf row per symbol."""
+    name: str
+    variant: str
+    fp: int
+    bypass: bool
+    bp: int
+    symbols: torch.Tensor     # (T,) int32
+    row_starts: torch.Tensor  # (B + 1,) int64
+    cdfs: torch.Tensor        # (T, A + 1) int32, row i for symbol i
+    cdfs_sizes: torch.Tensor  # (T,) int32
+    offsets: torch.Tensor     # (T,) int32
+    lookup: str = "search"
+
+    @property
+    def num_symbols(self) -> int:
+        return self.symbols.numel()
+
+    @property
+    def num_streams(self) -> int:
+        return self.row_starts.numel() - 1
+
+
+def ragged_lengths(streams: int, length_scale: float, seed: int) -> torch.Tensor:
+    """Stream lengths clamp(round(exp(N(ln 32768, 1))), 1024, 524288), scaled by length_scale."""
+    g = _gen("cpu", seed)
+    ln = torch.empty(streams, dtype=torch.float64).normal_(math.log(32768.0), 1.0, generator=g)
+    lo, hi = max(1, round(1024 * length_scale)), max(1, round(524288 * length_scale))
+    return torch.clamp(torch.round(torch.exp(ln) * length_scale), lo, hi).to(torch.int64)
+
+
+def ragged_adaptive(device="cuda", scale: float = 1.0, length_scale: float = 1.0, seed: int = 4,
+                    chunk_rows: int = 1 << 22) -> RaggedWorkload:
+    """rans32, 4,096 streams of lognormal lengths, each symbol with its own 33-entry cdf row
+    (softmax of N(0, 2^2) logits over 32 symbols, exact integer quantisation to 2^16), symbols
+    drawn from their rows.  Rows are generated on `device` in chunks of `chunk_rows`."""
+    fp, A = 16, 32
+    B = max(1, int(4096 * scale))
+    lengths = ragged_lengths(B, length_scale, seed)
+    rows = torch.zeros(B + 1, dtype=torch.int64)
+    rows[1:] = torch.cumsum(lengths, 0)
+    T = int(rows[-1])
+    cdfs = torch.empty((T, A + 1), dtype=torch.int32, device=device)
+    syms = torch.empty(T, dtype=torch.int32, device=device)
+    g = _gen(device, seed + 1)
+    for c0 in range(0, T, chunk_rows):
+        n = min(chunk_rows, T - c0)
+        logits = torch.randn((n, A), generator=g, device=device, dtype=torch.float64) * 2.0
+        cdf = quantize_pmf(torch.softmax(logits, -1), fp)
+        cdfs[c0:c0 + n] = cdf.to(torch.int32)
+        u = torch.randint(0, 1 << fp, (n, 1), generator=g, device=device, dtype=torch.int64)
+        syms[c0:c0 + n] = (torch.searchsorted(cdf, u, right=True) - 1).squeeze(1).to(torch.int32)
+        del logits, cdf, u
+    return RaggedWorkload("ragged_adaptive", "rans32", fp, False, 4, syms, rows.to(device), cdfs,
+                          torch.full((T,), A + 1, dtype=torch.int32, device=device),
+                          torch.zeros(T, dtype=torch.int32, device=device))
+
+
 BUILDERS = {
     "laplace64": laplace64,
     "gaussian_latent": gaussian_latent,
     "zipf_alias": zipf_alias,
     "mixture_invcdf": mixture_invcdf,
+    "ragged_adaptive": ragged_adaptive,
 }
