@@ -68,7 +68,7 @@ def dist_setup():
     if ws > 1:
         torch.cuda.set_device(local)
         from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local))
+        dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=torch.device("cuda", local))
     elif torch.cuda.is_available():
         torch.cuda.set_device(0)
     return ws, rank, local
@@ -270,10 +270,9 @@ def run_e2e(args, w, ws, rank, dev, _C, push, pop, init_cpu, push_t, pop_t, kw):
     def once():
         nonlocal h2d, d2h
         packed = coder.encode(h_sym, h_idx)
-        if ws > 1:  # place this rank's records in the job-wide bitstream
-            n_local = torch.tensor([packed.numel()], dtype=torch.int64, device=dev)
-            sizes = [torch.zeros_like(n_local) for _ in range(ws)]
-            dist.all_gather(sizes, n_local)
+        if ws > 1:  # place this rank's records in the job-wide bitstream (sizes all-gather, NCCL)
+            from torch_ans_b200.sharding import record_offsets
+            record_offsets(packed.numel(), device=dev)
         coder.decode(packed, h_idx, out=h_out)
         h2d = 2 * B * N * 4 + B * N * 4 + packed.numel()
         d2h = packed.numel() + B * N * 4
