@@ -500,13 +500,17 @@ static LaunchShape lean_shape(int64_t streams, int sms) {
   return L;
 }
 
-// TORCH_ANS_B200_POP_KERNEL: "lean" (default), "fast" (several streams per thread) or "generic"
+// TORCH_ANS_B200_POP_KERNEL: unset = the lean kernel for tables in L2 read per step (bucket,
+// split), the fast kernel for tables in shared memory and the fused table (short table latency,
+// so per-step overhead dominates and its branch-free chunks measured faster); "lean", "fast"
+// (several streams per thread) or "generic" force one
 static int pop_kernel_choice() {
   const char* e = std::getenv("TORCH_ANS_B200_POP_KERNEL");
   if (!e || !*e) return 0;
   const std::string v(e);
   if (v == "fast") return 1;
   if (v == "generic") return 2;
+  if (v == "lean") return 3;
   return 0;
 }
 
@@ -546,7 +550,7 @@ int pop_impl(int variant, int lookup, int interleave, int32_t* stream, int64_t b
   bool tin_smem = false;
   const int kchoice = pop_kernel_choice();
   const int ov = kchoice == 2 ? 100 : layout_override();
-  const bool lean = kchoice == 0;
+  bool lean = kchoice == 0 || kchoice == 3;
   if (use_tables && ov != 100 && nsym % 4 == 0 && vec_idx && vec_out && nsym / 4 < 0x7fffffff) {
     L = lean ? lean_shape(batch, dev_sms) : fast_shape(batch, dev_sms, spt);
     const int64_t ring = lean ? 0 : (int64_t)(L.threads / 32) * L.lanes * POPF_RS * 16 * spt;
@@ -579,7 +583,22 @@ int pop_impl(int variant, int lookup, int interleave, int32_t* stream, int64_t b
           break;
         }
     }
-    if (tm >= 0) smem = (size_t)ring + (size_t)popf_table_smem(tm, ntables, fp, cdf_width, sstride);
+    if ((tm == TM_FUSED_GLOBAL || tm == TM_FUSED_SMEM || tm == TM_SPLIT_SMEM) && kchoice == 0) {
+      // the fast kernel for this layout; its index ring must fit beside the table info too
+      int spt2 = 1;
+      const LaunchShape L2 = fast_shape(batch, dev_sms, spt2);
+      const int64_t ring2 = (int64_t)(L2.threads / 32) * L2.lanes * POPF_RS * 16 * spt2;
+      if (ring2 + popf_table_smem(tm, ntables, fp, cdf_width, sstride) <= kSmemBudget) {
+        lean = false;
+        L = L2;
+        spt = spt2;
+        smem = (size_t)ring2 + (size_t)popf_table_smem(tm, ntables, fp, cdf_width, sstride);
+      } else {
+        smem = (size_t)ring + (size_t)popf_table_smem(tm, ntables, fp, cdf_width, sstride);
+      }
+    } else if (tm >= 0) {
+      smem = (size_t)ring + (size_t)popf_table_smem(tm, ntables, fp, cdf_width, sstride);
+    }
   }
   const bool fast = tm >= 0;
   const bool need_fused = fast ? (tm == TM_FUSED_SMEM || tm == TM_FUSED_GLOBAL)
