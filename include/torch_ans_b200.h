@@ -155,6 +155,17 @@ int tans_pop_ragged(int variant, int32_t* stream, int64_t batch, int64_t stream_
                     const int32_t* offsets, int freq_precision, int bypass_coding, int bypass_precision,
                     uint32_t* dev_status, void* cuda_stream);
 
+/* Alias tables on the device: rans_alias_build_table (torch_ans/rans.cpp:56-95, build_alias_mapping
+ * torch_ans/rans_utils.hpp:537-651) for cdf rows already on the GPU.  remap_out [num_tables,
+ * cdf_width + 2^freq_precision] and table_out [num_tables, 5 cdf_width] are written whole (cdf
+ * prefix, then the remap / alias elements, zeros elsewhere), exactly as the reference builds them,
+ * including the rows it leaves unbuilt when its power-of-two cut condition fails.  workspace:
+ * tans_alias_workspace_size() bytes or NULL (allocated stream-ordered). */
+size_t tans_alias_workspace_size(int64_t num_tables, int symbol_precision);
+int tans_alias_build_table(const int32_t* cdfs, int64_t num_tables, int64_t cdf_width, const int32_t* cdf_sizes,
+                           int symbol_precision, int freq_precision, int32_t* remap_out, int32_t* table_out,
+                           void* workspace, size_t workspace_bytes, void* cuda_stream);
+
 /* Maximum of column 0 (payload length) over the batch rows, written to *out_max (device int32).
  * The device half of the worst-case resize at torch_ans/rans.hpp:105-107. */
 int tans_stream_max_length(const int32_t* stream, int64_t batch, int64_t stream_width,

@@ -511,3 +511,60 @@ def test_pop_heavy_tails_and_overrun(C, kernel, layout, lookup, variant, monkeyp
     assert C.device_status() == derr
     assert np.array_equal(dec.cpu().numpy(), dec_ref)
     assert same_rows(st.cpu().numpy(), ref_pop)
+
+
+@pytest.mark.parametrize("case", ["valid", "not_power_of_two", "bad_sum", "oversize", "mixed"])
+def test_alias_build_on_device_matches_host(C, case):
+    """rans_alias_build_table on CUDA tables (the device builder, tans_alias_build_table) returns
+    exactly the host builder's remap and table rows -- the rows the reference builds, including the
+    partial or empty rows of tables whose cut condition fails."""
+    rng = np.random.default_rng(zlib.crc32(f"alias-dev-{case}".encode()))
+    fp, sp = 12, 5
+    K, A = 6, 1 << sp
+    pm = rng.random((K, A)) + 0.02
+    cdfs = O.pmf_to_quantized_cdf((pm / pm.sum(1, keepdims=True)).astype(np.float32), fp)
+    sizes = np.full(K, A + 1, np.int32)
+    if case == "not_power_of_two":
+        sizes[:] = A  # A - 1 symbols: the cut does not divide 2^fp into 2^sp cuts
+    elif case == "bad_sum":
+        cdfs[:, -1] -= 3
+    elif case == "oversize":
+        sizes[1] = cdfs.shape[1] + 5
+        sizes[2] = -1
+    elif case == "mixed":
+        sizes[0] = A
+        cdfs[3, -1] += 1
+    host_remap, host_tab = C.rans_alias_build_table(torch.from_numpy(cdfs), torch.from_numpy(sizes), sp, fp)
+    dev_remap, dev_tab = C.rans_alias_build_table(t(cdfs), t(sizes), sp, fp)
+    assert dev_remap.is_cuda and dev_tab.is_cuda
+    assert torch.equal(dev_remap.cpu(), host_remap) and torch.equal(dev_tab.cpu(), host_tab)
+    if case == "valid":
+        g_remap, g_tab, ok = O.alias_build_table(cdfs, sizes, sp, fp)
+        assert ok == K and np.array_equal(host_remap.numpy(), g_remap) and np.array_equal(host_tab.numpy(), g_tab)
+
+
+def test_alias_build_on_device_golden():
+    """The golden alias tables made by the compiled reference, rebuilt on the device."""
+    import glob
+    import json
+    import os
+    from torch_ans_b200 import _C
+    checked = 0
+    for name in [n for n in G.coding_cases() if "alias" in n]:
+        d = G.load(name)
+        m = d["meta"]
+        w = int(d["sizes"].max()) - 1  # the golden cases use one cut per symbol
+        sp = int(np.log2(w))
+        if (1 << sp) != w:
+            continue
+        remap, tab = _C.rans_alias_build_table(t(d["cdfs"]), t(d["sizes"]), sp, int(m["fp"]))
+        assert np.array_equal(remap.cpu().numpy(), d["push_cdfs"]) and np.array_equal(tab.cpu().numpy(), d["pop_cdfs"])
+        checked += 1
+    here = os.path.join(os.path.dirname(__file__), "golden")
+    for path in sorted(glob.glob(os.path.join(here, "*_alias_rejected.npz"))):
+        z = np.load(path)
+        meta = json.loads(str(z["meta"]))
+        remap, tab = _C.rans_alias_build_table(t(z["cdfs"]), t(z["sizes"]), meta["sp"], meta["fp"])
+        assert np.array_equal(remap.cpu().numpy(), z["remap"]) and np.array_equal(tab.cpu().numpy(), z["table"])
+        checked += 1
+    assert checked >= 6

@@ -37,6 +37,8 @@ _SIGS = {
     "tans_scatter_payloads": ([_P, _P, _P, _P, _I64, _I64, _P], _I),
     "tans_cdf_fix_zero_freqs": ([_P, _I64, _I64, _P, _P], _I),
     "tans_push_ragged_workspace_size": ([_I64], _SZ),
+    "tans_alias_workspace_size": ([_I64, _I], _SZ),
+    "tans_alias_build_table": ([_P, _I64, _I64, _P, _I, _I, _P, _P, _P, _SZ, _P], _I),
     "tans_push_ragged": ([_I, _P, _I64, _I64, _P, _P, _P, _I64, _P, _I64, _I64, _P, _P, _I, _I, _I, _P, _SZ, _P, _P],
                          _I),
     "tans_pop_ragged": ([_I, _P, _I64, _I64, _P, _P, _P, _I64, _P, _I64, _I64, _P, _P, _I, _I, _I, _P, _P], _I),

@@ -591,11 +591,11 @@ Tensor pmf_to_quantized_cdf(const Tensor& pmfs, int64_t precision) {
 // rans_alias_build_table (torch_ans/rans.cpp:56-95, build_alias_mapping rans_utils.hpp:537-651):
 // Vose-style alias table over 2^symbol_precision equal cuts of 2^fp / (cdf_size - 1).  Host code
 // (it runs once per table set); the result is placed on the input's device.
-bool build_alias_row(const int32_t* cdf, int32_t cdf_size, int32_t* tab, int32_t* remap, int64_t sp, int64_t fp,
-                     int64_t tab_cap, int64_t remap_cap) {
+bool build_alias_row(const int32_t* cdf, int32_t cdf_size, int64_t cdf_width, int32_t* tab, int32_t* remap, int64_t sp,
+                     int64_t fp, int64_t tab_cap, int64_t remap_cap) {
   const int32_t nsym = cdf_size - 1;
   const int32_t total_range = 1 << fp;
-  if (nsym <= 0) return false;
+  if (nsym <= 0 || cdf_size > cdf_width) return false;  // a size past the row reads nothing outside it
   const int32_t cut = total_range / nsym;
   const int32_t ncuts = 1 << sp;
   if ((int64_t)ncuts * cut != total_range || ncuts < nsym) return false;
@@ -644,7 +644,7 @@ bool build_alias_row(const int32_t* cdf, int32_t cdf_size, int32_t* tab, int32_t
     const bool hi = r >= tab[4 * id];
     const int32_t sidx = hi ? tab[4 * id + 1] : id;
     const int32_t a0 = hi ? tab[4 * id + 3] : tab[4 * id + 2];
-    const int64_t at = (int64_t)r - a0 + cdf[sidx];
+    const int64_t at = (int64_t)r - a0 + ((sidx >= 0 && sidx < cdf_width) ? cdf[sidx] : 0);
     if (at >= 0 && at < remap_cap) remap[at] = r;
   }
   return true;
@@ -653,6 +653,26 @@ bool build_alias_row(const int32_t* cdf, int32_t cdf_size, int32_t* tab, int32_t
 std::tuple<Tensor, Tensor> alias_build_table(const Tensor& cdfs, const Tensor& cdfs_sizes, int64_t symbol_precision,
                                              int64_t freq_precision) {
   TORCH_CHECK(cdfs.dim() == 2 && cdfs.scalar_type() == torch::kInt32, "cdfs must be int32 (K, W)");
+  TORCH_CHECK(freq_precision >= 1 && freq_precision <= 31 && symbol_precision >= 0 && symbol_precision <= 24,
+              "bad precision");
+  if (cdfs.is_cuda()) {  // tables on the GPU are built there (tans_alias_build_table)
+    const at::Device dev = cdfs.device();
+    c10::cuda::CUDAGuard guard(dev);
+    Tensor c = cdfs.contiguous();
+    Tensor sz = cdfs_sizes.to(dev, torch::kInt32).contiguous();
+    TORCH_CHECK(sz.numel() == c.size(0), "cdfs_sizes must have one entry per cdf row");
+    const int64_t K = c.size(0), Wc = c.size(1);
+    const int64_t rw = Wc + ((int64_t)1 << freq_precision), tw = Wc * 5;
+    Tensor remap = torch::empty({K, rw}, c.options());
+    Tensor table = torch::empty({K, tw}, c.options());
+    Tensor ws = torch::empty({(int64_t)tans_alias_workspace_size(K, (int)symbol_precision) + 256},
+                             torch::TensorOptions().dtype(torch::kUInt8).device(dev));
+    check_rc(tans_alias_build_table(c.data_ptr<int32_t>(), K, Wc, sz.data_ptr<int32_t>(), (int)symbol_precision,
+                                    (int)freq_precision, remap.data_ptr<int32_t>(), table.data_ptr<int32_t>(),
+                                    ws.data_ptr(), (size_t)ws.numel(), cur_stream()),
+             "alias table build");
+    return {remap, table};
+  }
   Tensor c = cdfs.cpu().contiguous();
   Tensor sz = cdfs_sizes.cpu().to(torch::kInt32).contiguous();
   const int64_t K = c.size(0), Wc = c.size(1);
@@ -664,14 +684,14 @@ std::tuple<Tensor, Tensor> alias_build_table(const Tensor& cdfs, const Tensor& c
   at::parallel_for(0, K, 1, [&](int64_t b0, int64_t b1) {
     for (int64_t k = b0; k < b1; ++k) {
       const int32_t n = sp[k];
+      const int64_t nc = n < 0 ? 0 : std::min<int64_t>(n, Wc);
       int32_t* rr = remap.data_ptr<int32_t>() + k * rw;
       int32_t* tr = table.data_ptr<int32_t>() + k * tw;
-      std::memcpy(rr, cp + k * Wc, sizeof(int32_t) * n);
-      std::memcpy(tr, cp + k * Wc, sizeof(int32_t) * n);
-      build_alias_row(cp + k * Wc, n, tr + n, rr + n, symbol_precision, freq_precision, (tw - n) / 4, rw - n);
+      std::memcpy(rr, cp + k * Wc, sizeof(int32_t) * nc);
+      std::memcpy(tr, cp + k * Wc, sizeof(int32_t) * nc);
+      build_alias_row(cp + k * Wc, n, Wc, tr + nc, rr + nc, symbol_precision, freq_precision, (tw - nc) / 4, rw - nc);
     }
   });
-  if (cdfs.is_cuda()) return {remap.to(cdfs.device()), table.to(cdfs.device())};
   return {remap, table};
 }
 

@@ -31,7 +31,7 @@ constexpr int POPF_L = 6;   // chunks between an index load and its use
 inline int64_t popf_table_smem(int tm, int64_t ntables, int fp, int64_t cdf_width, int64_t st_stride) {
   (void)cdf_width;
   const int64_t m = ntables << fp;
-  const int64_t info = ntables * 24;  // TableInfo + {offset, escape slot}
+  const int64_t info = ntables * 32;  // TableInfo + a 16-byte per-table record of the kernels
   switch (tm) {
     case TM_FUSED_SMEM: return info + m * 4 + m * 2 + 16;
     case TM_SPLIT_SMEM: return info + ntables * st_stride * 4 + m * 2 + 16;
