@@ -460,7 +460,8 @@ def cpu_reference(workload_name, seconds, scale, length_scale, steps=1, warmup=0
     kind = "reference" if ref is not None else "port"
     threads = len(os.sched_getaffinity(0))
     torch.set_num_threads(threads)
-    probe = build_workload(workload_name, "cpu", scale=scale, length_scale=length_scale)
+    # the stream count of the full configuration, from a probe with one-symbol streams
+    probe = build_workload(workload_name, "cpu", scale=scale, length_scale=1e-9)
     b_full = probe.symbols.shape[0]
     del probe
 
@@ -497,6 +498,10 @@ def cpu_reference(workload_name, seconds, scale, length_scale, steps=1, warmup=0
     tp, tq = run(w)
     per_stream = (tp + tq) / n
     n2 = int(min(b_full, max(n, seconds / max(per_stream, 1e-9))))
+    # at most 2^28 symbols (2 GiB of host symbols + indexes) per sample, so the sample's build and
+    # the whole reference run stay within a few minutes on any host
+    N_full = w.symbols.shape[1]
+    n2 = max(n, min(n2, (1 << 28) // max(N_full, 1)))
     if n2 >= threads:
         n2 = n2 // threads * threads
     if n2 > n:
@@ -526,7 +531,7 @@ def main():
     ragged = args.workload == "ragged_adaptive"
     if args.impl == "reference":
         if rank == 0:
-            per_step = max(2.0, 150.0 / max(1, args.steps + args.warmup))
+            per_step = min(10.0, max(2.0, 120.0 / max(1, args.steps + args.warmup)))
             if ragged:
                 base = cpu_reference_ragged(per_step * 4, args.scale, args.length_scale)
             else:
