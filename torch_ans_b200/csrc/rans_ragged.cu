@@ -287,45 +287,49 @@ constexpr int RW_D = 12;   // steps between a row copy and its use
 constexpr int RW_R = 16;   // row ring slots per warp (> RW_D)
 constexpr int RW_E = 66;   // staged words per slot: 64 entries + size + offset
 
-template <int V, bool BYPASS>
+template <int V, bool BYPASS, bool WIDE>
 __global__ void __launch_bounds__(256) ragged_pop_warp_kernel(const RaggedArgs R, const PopParams P) {
   using S = typename VT<V>::State;
+  using Wd = typename VT<V>::Word;
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const int warps = blockDim.x >> 5, wib = threadIdx.x >> 5, lane = threadIdx.x & 31;
   int32_t* ring = reinterpret_cast<int32_t*>(smem_raw) + (size_t)wib * RW_R * RW_E;
   const int64_t b = (int64_t)blockIdx.x * warps + wib;
   if (b >= R.batch) return;
   int64_t lo, hi;
-  if (!ragged_row(R, b, lo, hi)) {
+  if (!ragged_row(R, b, lo, hi) || hi - lo > 0x7fffff00) {
     if (lane == 0) report(R.status, DEV_BAD_VALUE);
     return;
   }
   int32_t* row = R.stream + b * R.width;
-  PopCursor<V> cur;
-  cur.payload = reinterpret_cast<const uint8_t*>(row + 1);
-  cur.p = (int64_t)row[0] / VT<V>::WBYTES - 1;
-  cur.first = VT<V>::SBYTES / VT<V>::WBYTES;
-  cur.cap = (R.width - 1) * 4 / VT<V>::WBYTES;
-  cur.err = 0;
+  // word cursor (every lane holds the same copy): next word index p, its word prefetched in nextw
+  const Wd* pw = reinterpret_cast<const Wd*>(row + 1);
+  const int64_t p64 = (int64_t)row[0] / VT<V>::WBYTES - 1;
+  const int first = VT<V>::SBYTES / VT<V>::WBYTES;
+  const int capw = (int)min((R.width - 1) * 4 / VT<V>::WBYTES, (int64_t)0x7fffffff);
+  int p = (int)min(max(p64, (int64_t)-0x7fffffff), (int64_t)0x7fffffff);
+  S nextw = (p >= first && p < capw) ? (S)__ldg(pw + p) : (S)0;
+  uint32_t err = 0;
   S x = load_state<V>(row, 0);
-  const int64_t n = hi - lo;
+  const int n = (int)(hi - lo);
   const int W = (int)R.cdf_width;
+  const int32_t cmask = (int32_t)((1u << R.fp) - 1u);
   int32_t kcur = 0;   // table index held by this lane for steps [32 m, 32 m + 32)
   int32_t outv = 0;   // decoded symbol of step 32 m + lane
-  auto table_at = [&](int64_t t, int32_t kreg) -> int64_t {
-    return R.idx ? (int64_t)__shfl_sync(0xffffffffu, kreg, (int)(t & 31)) : lo + t;
+  auto table_at = [&](int t, int32_t kreg) -> int64_t {
+    return R.idx ? (int64_t)__shfl_sync(0xffffffffu, kreg, t & 31) : lo + t;
   };
-  int32_t kahead = (R.idx && lane < n) ? R.idx[lo + lane] : 0;      // indexes of steps [0, 32)
+  int32_t kahead = (R.idx && lane < n) ? R.idx[lo + lane] : 0;           // indexes of steps [0, 32)
   int32_t kahead2 = (R.idx && 32 + lane < n) ? R.idx[lo + 32 + lane] : 0;  // steps [32, 64)
   // iteration j: stage the row of step j, decode step j - RW_D
-  for (int64_t j = 0; j < n + RW_D; ++j) {
+  for (int j = 0; j < n + RW_D; ++j) {
     if ((j & 31) == 0 && j > 0) {  // rotate the index registers every 32 steps
       kahead = kahead2;
       kahead2 = (R.idx && j + 32 + lane < n) ? R.idx[lo + j + 32 + lane] : 0;
     }
     if (j < n) {
       const int64_t k = table_at(j, kahead);
-      int32_t* slot = ring + (int)(j & (RW_R - 1)) * RW_E;
+      int32_t* slot = ring + (j & (RW_R - 1)) * RW_E;
       if (k >= 0 && k < R.ntables) {
         const int32_t* src = R.cdfs + k * R.cdf_width;
         if (lane < W) cp_async4(slot + lane, src + lane);
@@ -337,7 +341,7 @@ __global__ void __launch_bounds__(256) ragged_pop_warp_kernel(const RaggedArgs R
       }
     }
     cp_async_commit();
-    const int64_t tc = j - RW_D;
+    const int tc = j - RW_D;
     if (tc < 0) continue;
     if ((tc & 31) == 0) {
       if (tc > 0) R.out[lo + tc - 32 + lane] = outv;  // the previous 32 steps: one coalesced store
@@ -349,61 +353,108 @@ __global__ void __launch_bounds__(256) ragged_pop_warp_kernel(const RaggedArgs R
     const int64_t k = table_at(tc, kcur);
     int32_t v = 0;
     if (k < 0 || k >= R.ntables) {
-      cur.err |= DEV_BAD_INDEX;
+      err |= DEV_BAD_INDEX;
     } else {
-      const int32_t* slot = ring + (int)(tc & (RW_R - 1)) * RW_E;
-      TableInfo tinf;
-      tinf.size = __shfl_sync(0xffffffffu, lane == 0 ? slot[64] : 0, 0);
-      tinf.offset = R.offsets ? __shfl_sync(0xffffffffu, lane == 0 ? slot[65] : 0, 0) : 0;
-      tinf.cut = 0;
-      tinf.cut_log2 = -1;
-      const int32_t size = tinf.size;
-      const int32_t cum = (int32_t)(uint32_t)(x & (S)((1ull << R.fp) - 1ull));
+      const int32_t* slot = ring + (tc & (RW_R - 1)) * RW_E;
+      const int32_t size = __shfl_sync(0xffffffffu, lane == 0 ? slot[64] : 0, 0);
+      const int32_t offset = R.offsets ? __shfl_sync(0xffffffffu, lane == 0 ? slot[65] : 0, 0) : 0;
+      const int32_t cum = (int32_t)((uint32_t)x & (uint32_t)cmask);
       const int32_t c0 = lane < W ? slot[lane] : 0;
-      const int32_t c1 = lane + 32 < W ? slot[32 + lane] : 0;
-      // fast path: 2 <= size <= W, row non-decreasing on [0, size), row[0] <= cum < row[size - 1]
-      const int32_t n0 = __shfl_down_sync(0xffffffffu, c0, 1);
-      const int32_t c1_first = __shfl_sync(0xffffffffu, c1, 0);
-      const int32_t n1 = __shfl_down_sync(0xffffffffu, c1, 1);
-      const int32_t next0 = lane == 31 ? c1_first : n0;
-      const bool mono = (lane + 1 >= size || c0 <= next0) && (lane + 33 >= size || c1 <= n1);
-      const int32_t last = size >= 1 && size <= 64 ? __shfl_sync(0xffffffffu, size - 1 < 32 ? c0 : c1, (size - 1) & 31)
-                                                    : 0;
-      const int32_t first = __shfl_sync(0xffffffffu, c0, 0);
-      const bool fast = size >= 2 && size <= W && __all_sync(0xffffffffu, mono) && first <= cum && cum < last;
       int64_t s;
-      int32_t cum_off, freq;
+      int32_t cum_off = 0, freq = 0;
       bool found;
+      bool fast;
+      int32_t st = 0, en = 0;
+      if constexpr (!WIDE) {
+        // rows of at most 33 entries: lane l holds entry l, every lane reads entry 32
+        const int32_t e32 = W > 32 ? slot[32] : 0;
+        const int32_t n0 = __shfl_down_sync(0xffffffffu, c0, 1);
+        const int32_t next0 = lane == 31 ? e32 : n0;
+        const bool mono = lane + 1 >= size || c0 <= next0;
+        const int32_t lastv = size - 1 == 32 ? e32 : __shfl_sync(0xffffffffu, c0, (size - 1) & 31);
+        const int32_t firstv = __shfl_sync(0xffffffffu, c0, 0);
+        fast = size >= 2 && size <= W && __all_sync(0xffffffffu, mono) && firstv <= cum && cum < lastv;
+        if (fast) {
+          s = __popc(__ballot_sync(0xffffffffu, lane < size - 1 && c0 <= cum)) - 1;
+          st = __shfl_sync(0xffffffffu, c0, (int)s);
+          const int32_t en0 = __shfl_sync(0xffffffffu, c0, (int)(s + 1) & 31);
+          en = s + 1 == 32 ? e32 : en0;
+        }
+      } else {
+        const int32_t c1 = lane + 32 < W ? slot[32 + lane] : 0;
+        const int32_t n0 = __shfl_down_sync(0xffffffffu, c0, 1);
+        const int32_t c1_first = __shfl_sync(0xffffffffu, c1, 0);
+        const int32_t n1 = __shfl_down_sync(0xffffffffu, c1, 1);
+        const int32_t next0 = lane == 31 ? c1_first : n0;
+        const bool mono = (lane + 1 >= size || c0 <= next0) && (lane + 33 >= size || c1 <= n1);
+        const int32_t lastv =
+            size >= 1 && size <= 64 ? __shfl_sync(0xffffffffu, size - 1 < 32 ? c0 : c1, (size - 1) & 31) : 0;
+        const int32_t firstv = __shfl_sync(0xffffffffu, c0, 0);
+        fast = size >= 2 && size <= W && __all_sync(0xffffffffu, mono) && firstv <= cum && cum < lastv;
+        if (fast) {
+          const unsigned m0 = __ballot_sync(0xffffffffu, lane < size - 1 && c0 <= cum);
+          const unsigned m1 = __ballot_sync(0xffffffffu, lane + 32 < size - 1 && c1 <= cum);
+          s = __popc(m0) + __popc(m1) - 1;
+          st = __shfl_sync(0xffffffffu, s < 32 ? c0 : c1, (int)(s & 31));
+          en = __shfl_sync(0xffffffffu, s + 1 < 32 ? c0 : c1, (int)((s + 1) & 31));
+        }
+      }
       if (fast) {
-        const unsigned m0 = __ballot_sync(0xffffffffu, lane < size - 1 && c0 <= cum);
-        const unsigned m1 = __ballot_sync(0xffffffffu, lane + 32 < size - 1 && c1 <= cum);
-        const int cnt = __popc(m0) + __popc(m1);
-        s = cnt - 1;
-        const int32_t st = __shfl_sync(0xffffffffu, s < 32 ? c0 : c1, (int)(s & 31));
-        const int32_t en = __shfl_sync(0xffffffffu, s + 1 < 32 ? c0 : c1, (int)((s + 1) & 31));
         cum_off = cum - st;
         freq = (int32_t)((uint32_t)en - (uint32_t)st);
         found = true;
       } else {
+        TableInfo tinf;
+        tinf.size = size;
+        tinf.offset = offset;
+        tinf.cut = 0;
+        tinf.cut_log2 = -1;
         found = lookup_symbol<V, LK_SEARCH, false>(slot, tinf, cum, R.cdf_width, R.fp, s, cum_off, freq);
       }
       if (!found) {
-        cur.err |= DEV_BAD_VALUE;
+        err |= DEV_BAD_VALUE;
       } else {
-        const int32_t d = pop_finish<V, BYPASS>(P, x, cur, (int32_t)s, cum_off, freq, size - 2);
-        v = (int32_t)((uint32_t)d + (uint32_t)tinf.offset);
+        // x = D(x) and the refill (rans_utils.hpp:473-475), the first word from the prefetch
+        x = (S)((x >> R.fp) * to_state<S>(freq) + to_state<S>(cum_off));
+#pragma unroll
+        for (int t = 0; t < VT<V>::MAX_RENORM; ++t) {
+          if ((unsigned long long)x < VT<V>::LB) {
+            if (p < first || p >= capw) err |= DEV_UNDERFLOW;
+            x = (S)((x << VT<V>::WB) | nextw);
+            --p;
+            nextw = (p >= first && p < capw) ? (S)__ldg(pw + p) : (S)0;
+          }
+        }
+        int32_t value = (int32_t)s;
+        if constexpr (BYPASS) {
+          if (value == size - 2) {  // escape (rare): the cursor-based reference code
+            PopCursor<V> cur;
+            cur.payload = reinterpret_cast<const uint8_t*>(row + 1);
+            cur.p = p;
+            cur.first = first;
+            cur.cap = (R.width - 1) * 4 / VT<V>::WBYTES;
+            cur.err = err;
+            const int32_t raw = pop_escape<V>(x, cur, R.bp);
+            value = raw >> 1;
+            value = (raw & 1) ? (-value - 1) : (value + size - 2);
+            p = (int)min(max(cur.p, (int64_t)-0x7fffffff), (int64_t)0x7fffffff);
+            err = cur.err;
+            nextw = (p >= first && p < capw) ? (S)__ldg(pw + p) : (S)0;
+          }
+        }
+        v = (int32_t)((uint32_t)value + (uint32_t)offset);
       }
     }
-    if ((int)(tc & 31) == lane) outv = v;
+    if ((tc & 31) == lane) outv = v;
   }
   // the last group of decoded symbols (full or partial)
-  const int64_t last = n > 0 ? ((n - 1) & ~(int64_t)31) : 0;
+  const int last = n > 0 ? ((n - 1) & ~31) : 0;
   if (n > 0 && last + lane < n) R.out[lo + last + lane] = outv;
   cp_async_wait<0>();
   if (lane == 0) {
     store_state<V>(row, 0, x);
-    row[0] = (int32_t)((cur.p + 1) * VT<V>::WBYTES);
-    report(R.status, cur.err);
+    row[0] = (int32_t)((int64_t)(p + 1) * VT<V>::WBYTES);
+    report(R.status, err);
   }
 }
 
@@ -431,15 +482,21 @@ static void ragged_push_launch(const RaggedArgs& R, const PushParams& P, int sms
   note_launch();
 }
 
-template <int V, bool BY>
-static void ragged_pop_warp_launch(const RaggedArgs& R, const PopParams& P, int sms, cudaStream_t s) {
+template <int V, bool BY, bool WIDE>
+static void ragged_pop_warp_go(const RaggedArgs& R, const PopParams& P, int sms, cudaStream_t s) {
   int64_t warps = (R.batch + sms - 1) / sms;
   warps = std::max<int64_t>(1, std::min<int64_t>(warps, 8));
   const size_t smem = (size_t)warps * RW_R * RW_E * sizeof(int32_t);
   if (smem > 48 * 1024)
-    cudaFuncSetAttribute(ragged_pop_warp_kernel<V, BY>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  ragged_pop_warp_kernel<V, BY><<<(int)((R.batch + warps - 1) / warps), (int)(warps * 32), smem, s>>>(R, P);
+    cudaFuncSetAttribute(ragged_pop_warp_kernel<V, BY, WIDE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  ragged_pop_warp_kernel<V, BY, WIDE><<<(int)((R.batch + warps - 1) / warps), (int)(warps * 32), smem, s>>>(R, P);
   note_launch();
+}
+
+template <int V, bool BY>
+static void ragged_pop_warp_launch(const RaggedArgs& R, const PopParams& P, int sms, cudaStream_t s) {
+  if (R.cdf_width <= 33) ragged_pop_warp_go<V, BY, false>(R, P, sms, s);
+  else ragged_pop_warp_go<V, BY, true>(R, P, sms, s);
 }
 
 template <int V, bool BY, bool STAGE>
