@@ -236,12 +236,19 @@ def run_ours(args, ws, rank, local):
             traffic = ent["dram_bytes_per_symbol"] * nsym
     except Exception:
         pass
+    clocks = clk.summary()
+    # the kernels are bound by the latency of one serial step per stream: report it beside the
+    # bandwidth roofline (every stream runs its N steps concurrently with the others)
+    step_ns = dom_ms * 1e6 / max(N, 1)
+    step_cycles = step_ns * clocks["sm_mhz"] / 1e3 if clocks.get("sm_mhz") else None
     res = dict(value=value, ms=ms_max, gpu_launches=int(n_launch), push_ms=push_ms_max, pop_ms=pop_ms_max, ok=all_ok, nsym=nsym, B=B, N=N,
-               comp_bytes_per_symbol=c, clocks=clk.summary(),
+               comp_bytes_per_symbol=c, clocks=clocks,
                roofline={"bound": "hbm", "kernel": f"{w.pop_op if dom == 'pop' else w.push_op}",
                          "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                          "peak_kind": peak_kind, "traffic": traffic,
-                         "algorithmic_bytes_per_launch": alg[dom], "launch_ms": dom_ms},
+                         "algorithmic_bytes_per_launch": alg[dom], "launch_ms": dom_ms,
+                         "serial_step_ns": step_ns, "serial_step_cycles": step_cycles,
+                         "streams_in_flight": B},
                encode_gsym_s=total / (push_ms_max / 1e3) / 1e9, decode_gsym_s=total / (pop_ms_max / 1e3) / 1e9)
     if not args.no_e2e:
         res["e2e"] = run_e2e(args, w, ws, rank, dev, _C, push, pop, init_cpu, push_t, pop_t, kw)

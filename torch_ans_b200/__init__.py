@@ -5,16 +5,22 @@
 * ``torch_ans_b200.utils``: the CompressAI-like ``TorchANSInterface`` coder and its helpers.
 * ``torch_ans_b200.capi``: ctypes access to the C ABI library (include/torch_ans_b200.h).
 
-There is no CPU coding path: importing fails loudly when the native extension is missing, and
-coding ops raise on CPU tensors.
+There is no CPU coding path: using the package without its native extension fails loudly
+(``torch_ans_b200._C`` and every module that codes raise ImportError), and coding ops raise on
+CPU tensors.  Only ``torch_ans_b200.build`` works before the extension exists.
 """
 import torch as _torch  # noqa: F401  (loads libtorch before the extension)
 
 try:
     from . import _C  # noqa: F401
-except ImportError as e:  # pragma: no cover - exercised only when the build is missing
-    raise ImportError(
-        "torch_ans_b200 native extension is not built; run `python -m torch_ans_b200.build` "
-        f"(or __graft_entry__.build()). Original error: {e}") from e
+except ImportError as _e:  # the build step itself imports this package before _C exists
+    _IMPORT_ERROR = _e
+
+    def __getattr__(name):
+        if name == "_C":
+            raise ImportError(
+                "torch_ans_b200 native extension is not built; run `python -m torch_ans_b200.build` "
+                f"(or __graft_entry__.build()). Original error: {_IMPORT_ERROR}") from _IMPORT_ERROR
+        raise AttributeError(name)
 
 __all__ = ["_C"]
