@@ -262,12 +262,27 @@ def run_e2e(args, w, ws, rank, dev, _C, push, pop, init_cpu, push_t, pop_t, kw):
     pinned host symbols and indexes in, concatenated bitstream out to pinned host memory, then that
     bitstream and the indexes back in and the decoded symbols out (host wall clock, max over ranks)."""
     from torch_ans_b200.host_pipeline import HostStreamCoder
-    B, N = w.symbols.shape
+    B_all, N = w.symbols.shape
+    # pinned host buffers per rank: symbols, indexes, decoded symbols (4 B each) and the bitstream;
+    # every rank of this host gets an equal share of 40 % of the available host memory, and when
+    # the whole batch does not fit, the round trip runs on its first streams (same workload)
+    try:
+        import psutil
+        avail = psutil.virtual_memory().available
+    except Exception:
+        avail = 64 << 30
+    local_ws = int(os.environ.get("LOCAL_WORLD_SIZE", ws))
+    per_stream = N * (3 * 4 + 2)
+    B = int(max(1, min(B_all, (0.4 * avail / max(local_ws, 1)) // per_stream)))
+    if ws > 1:  # every rank codes the same number of streams
+        t = torch.tensor([B], dtype=torch.int64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MIN)
+        B = int(t.item())
     h_sym = torch.empty((B, N), dtype=torch.int32, pin_memory=True)
     h_idx = torch.empty((B, N), dtype=torch.int32, pin_memory=True)
     h_out = torch.empty((B, N), dtype=torch.int32, pin_memory=True)
-    h_sym.copy_(w.symbols)
-    h_idx.copy_(w.indexes)
+    h_sym.copy_(w.symbols[:B])
+    h_idx.copy_(w.indexes[:B])
     torch.cuda.synchronize()
     coder = HostStreamCoder(w.variant, push_t, pop_t, w.cdfs_sizes, w.offsets, freq_precision=w.fp,
                             bypass_coding=w.bypass, bypass_precision=w.bp, alias=w.push_cdfs is not None,
@@ -298,7 +313,7 @@ def run_e2e(args, w, ws, rank, dev, _C, push, pop, init_cpu, push_t, pop_t, kw):
     all_ok = max_over_ranks(0.0 if ok else 1.0, ws) == 0.0
     del h_sym, h_idx, h_out, coder
     return {"value": B * N * ws / el / 1e9, "unit": UNIT, "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
-            "ms_per_step": el * 1e3, "ok": all_ok,
+            "ms_per_step": el * 1e3, "ok": all_ok, "streams_per_gpu": B, "of_streams_per_gpu": B_all,
             "path": "pinned host -> HostStreamCoder.encode (column chunks: H2D || push) -> bitstream on host -> "
                     "HostStreamCoder.decode (H2D || pop || D2H) -> pinned host"}
 
