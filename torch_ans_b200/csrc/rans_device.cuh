@@ -224,6 +224,24 @@ __device__ __forceinline__ bool warp_wait(unsigned long long* b, unsigned parity
   return false;
 }
 
+// ---------------------------------------------------------------- TMA bulk copies (1D)
+// fence that makes a freshly initialised mbarrier visible to the asynchronous (TMA) proxy
+__device__ __forceinline__ void mbar_init_fence() {
+  asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+}
+// one arrival that also announces `bytes` of TMA transactions the phase must wait for
+__device__ __forceinline__ void mbar_arrive_expect_tx(unsigned long long* b, unsigned bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_u32(b)), "r"(bytes) : "memory");
+}
+// global -> shared bulk copy by the copy engine (both addresses 16-byte aligned, size a multiple of
+// 16); its bytes count against the mbarrier's transaction count.  No multicast.
+__device__ __forceinline__ void bulk_copy_g2s(void* smem, const void* gmem, unsigned bytes, unsigned long long* b) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
+                   smem_u32(smem)),
+               "l"(gmem), "r"(bytes), "r"(smem_u32(b))
+               : "memory");
+}
+
 // L2 eviction policies: tables that every step reads stay (evict_last); data read or written
 // once goes first (evict_first), so streaming rows do not push the tables out of L2.
 __device__ __forceinline__ unsigned long long policy_evict_last() {

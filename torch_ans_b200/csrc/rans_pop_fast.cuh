@@ -27,15 +27,75 @@ constexpr int kBucketBits = 4;  // bucket layout: 16 cum values per bucket
 constexpr int POPF_RS = 8;  // index ring slots (chunks of 4)
 constexpr int POPF_L = 6;   // chunks between an index load and its use
 
-// bytes of shared memory the tables of a layout occupy
+// bytes of shared memory the tables of a layout occupy (each region 16-byte aligned and padded to
+// a multiple of 16 bytes for the bulk copies)
 inline int64_t popf_table_smem(int tm, int64_t ntables, int fp, int64_t cdf_width, int64_t st_stride) {
   (void)cdf_width;
   const int64_t m = ntables << fp;
-  const int64_t info = ntables * 32;  // TableInfo + a 16-byte per-table record of the kernels
+  const int64_t info = ntables * 32;  // TableInfo + a per-table record of the kernels, padded
+  auto r16 = [](int64_t b) { return (b + 15) & ~(int64_t)15; };
   switch (tm) {
-    case TM_FUSED_SMEM: return info + m * 4 + m * 2 + 16;
-    case TM_SPLIT_SMEM: return info + ntables * st_stride * 4 + m * 2 + 16;
+    case TM_FUSED_SMEM: return info + r16(m * 4) + r16(m * 2) + 16;
+    case TM_SPLIT_SMEM: return info + r16(ntables * st_stride * 4) + r16(m * 2) + 16;
     default: return info;
+  }
+}
+
+// 16-byte aligned start of the table region after the per-table records
+__device__ __forceinline__ unsigned char* popf_align16(void* p) {
+  return reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(p) + 15) & ~(uintptr_t)15);
+}
+
+// Stage the shared-memory table layouts (fused D + S, or split ST + S) with 1D TMA bulk copies:
+// thread 0 announces the bytes on an mbarrier and issues the copies (popf_stage_begin), the copy
+// engine moves the tables while the block fills its per-table records, then every thread waits
+// for the phase with a bounded loop (popf_stage_end).  The regions are the workspace arrays
+// (256-byte aligned, padded) and 16-byte aligned shared regions, sizes rounded up to 16 bytes;
+// anything misaligned falls back to a thread copy.
+template <int TM>
+__device__ __forceinline__ void popf_stage_begin(const PopParams& P, uint32_t* tD, uint16_t* tS, int64_t m,
+                                                 unsigned long long* bar, int* use_tma) {
+  if constexpr (TM == TM_FUSED_SMEM || TM == TM_SPLIT_SMEM) {
+    const int T = blockDim.x, tid = threadIdx.x;
+    const void* srcA = TM == TM_FUSED_SMEM ? (const void*)P.fD : (const void*)P.fST;
+    const int64_t nA = TM == TM_FUSED_SMEM ? m : P.ntables * P.st_stride;  // 4-byte words of D / ST
+    const unsigned bytesA = (unsigned)((nA * 4 + 15) & ~(int64_t)15);
+    const unsigned bytesS = (unsigned)((m * 2 + 15) & ~(int64_t)15);
+    if (tid == 0) {
+      const bool ok = ((reinterpret_cast<uintptr_t>(srcA) | reinterpret_cast<uintptr_t>(P.fS)) & 15u) == 0 &&
+                      ((smem_u32(tD) | smem_u32(tS)) & 15u) == 0 && bytesA + bytesS < (1u << 20);
+      *use_tma = ok ? 1 : 0;
+      if (ok) {
+        mbar_init(bar, 1);
+        mbar_init_fence();
+        constexpr unsigned kChunk = 32768;
+        mbar_arrive_expect_tx(bar, bytesA + bytesS);
+        for (unsigned o = 0; o < bytesA; o += kChunk)
+          bulk_copy_g2s(reinterpret_cast<unsigned char*>(tD) + o, reinterpret_cast<const unsigned char*>(srcA) + o,
+                        min(kChunk, bytesA - o), bar);
+        for (unsigned o = 0; o < bytesS; o += kChunk)
+          bulk_copy_g2s(reinterpret_cast<unsigned char*>(tS) + o, reinterpret_cast<const unsigned char*>(P.fS) + o,
+                        min(kChunk, bytesS - o), bar);
+      }
+    }
+    __syncthreads();
+    if (!*use_tma) {
+      for (int64_t i = tid; i < nA; i += T) tD[i] = reinterpret_cast<const uint32_t*>(srcA)[i];
+      for (int64_t i = tid; i < m; i += T) tS[i] = P.fS[i];
+    }
+  }
+}
+
+// wait for the staged tables; false when the wait ran out (the caller reports TANS_DEV_STALLED)
+template <int TM>
+__device__ __forceinline__ bool popf_stage_end(unsigned long long* bar, const int* use_tma) {
+  if constexpr (TM == TM_FUSED_SMEM || TM == TM_SPLIT_SMEM) {
+    if (!*use_tma) return true;
+    for (unsigned it = 0; it < (1u << 20); ++it)
+      if (mbar_try_wait(bar, 0)) return true;
+    return false;
+  } else {
+    return true;
   }
 }
 
@@ -138,26 +198,27 @@ __global__ void __launch_bounds__(512) pop_fast_kernel(const PopParams P) {
   int4* ring = reinterpret_cast<int4*>(smem_raw);
   TableInfo* tsm = reinterpret_cast<TableInfo*>(ring + POPF_RS * nact * SPT);
   int2* tsm2 = reinterpret_cast<int2*>(tsm + P.ntables);  // {offset, escape slot} per table
-  unsigned char* tab = reinterpret_cast<unsigned char*>(tsm2 + P.ntables);
+  unsigned char* tab = popf_align16(tsm2 + P.ntables);
   const int64_t M = (int64_t)1 << P.fp;
   const int64_t m = P.ntables << P.fp;
   uint32_t* tD = reinterpret_cast<uint32_t*>(tab);  // fused: D; split: ST
   uint16_t* tS = reinterpret_cast<uint16_t*>(
-      tab + (TM == TM_FUSED_SMEM ? m * 4 : (TM == TM_SPLIT_SMEM ? P.ntables * P.st_stride * 4 : 0)));
+      tab + (((TM == TM_FUSED_SMEM ? m * 4 : (TM == TM_SPLIT_SMEM ? P.ntables * P.st_stride * 4 : 0)) + 15) &
+             ~(int64_t)15));
+  __shared__ unsigned long long stage_bar;
+  __shared__ int stage_tma;
+  popf_stage_begin<TM>(P, tD, tS, m, &stage_bar, &stage_tma);  // the copy engine runs while the records fill
   for (int64_t k = tid; k < P.ntables; k += T) {
     const TableInfo ti = P.tinfo[k];
     tsm[k] = ti;
     tsm2[k] = make_int2(ti.offset, ti.size - 2);
   }
-  if constexpr (TM == TM_FUSED_SMEM) {
-    for (int64_t i = tid; i < m; i += T) tD[i] = P.fD[i];
-    for (int64_t i = tid; i < m; i += T) tS[i] = P.fS[i];
-  } else if constexpr (TM == TM_SPLIT_SMEM) {
-    const int64_t n = P.ntables * P.st_stride;
-    for (int64_t i = tid; i < n; i += T) tD[i] = P.fST[i];
-    for (int64_t i = tid; i < m; i += T) tS[i] = P.fS[i];
-  }
+  const bool staged = popf_stage_end<TM>(&stage_bar, &stage_tma);
   __syncthreads();
+  if (!staged) {
+    if (threadIdx.x == 0) report(P.status, DEV_STALLED);
+    return;
+  }
   if (lane >= P.lanes) return;
 
   // streams of this thread; slots past the batch shadow the thread's first stream (same reads,

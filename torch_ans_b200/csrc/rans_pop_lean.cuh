@@ -67,26 +67,27 @@ __global__ void __launch_bounds__(512) pop_lean_kernel(const PopParams P) {
   const int warps = T >> 5, warp = tid >> 5, lane = tid & 31;
   TableInfo* tsm = reinterpret_cast<TableInfo*>(smem_raw);
   int2* tsm2 = reinterpret_cast<int2*>(tsm + P.ntables);  // {offset, escape slot} per table
-  unsigned char* tab = reinterpret_cast<unsigned char*>(tsm2 + P.ntables);
+  unsigned char* tab = popf_align16(tsm2 + P.ntables);
   const int64_t M = (int64_t)1 << P.fp;
   const int64_t m = P.ntables << P.fp;
   uint32_t* tD = reinterpret_cast<uint32_t*>(tab);  // fused: D; split: ST
   uint16_t* tS = reinterpret_cast<uint16_t*>(
-      tab + (TM == TM_FUSED_SMEM ? m * 4 : (TM == TM_SPLIT_SMEM ? P.ntables * P.st_stride * 4 : 0)));
+      tab + (((TM == TM_FUSED_SMEM ? m * 4 : (TM == TM_SPLIT_SMEM ? P.ntables * P.st_stride * 4 : 0)) + 15) &
+             ~(int64_t)15));
+  __shared__ unsigned long long stage_bar;
+  __shared__ int stage_tma;
+  popf_stage_begin<TM>(P, tD, tS, m, &stage_bar, &stage_tma);  // the copy engine runs while the records fill
   for (int64_t k = tid; k < P.ntables; k += T) {
     const TableInfo ti = P.tinfo[k];
     tsm[k] = ti;
     tsm2[k] = make_int2(ti.offset, BYPASS ? ti.size - 2 : -1);
   }
-  if constexpr (TM == TM_FUSED_SMEM) {
-    for (int64_t i = tid; i < m; i += T) tD[i] = P.fD[i];
-    for (int64_t i = tid; i < m; i += T) tS[i] = P.fS[i];
-  } else if constexpr (TM == TM_SPLIT_SMEM) {
-    const int64_t n = P.ntables * P.st_stride;
-    for (int64_t i = tid; i < n; i += T) tD[i] = P.fST[i];
-    for (int64_t i = tid; i < m; i += T) tS[i] = P.fS[i];
-  }
+  const bool staged = popf_stage_end<TM>(&stage_bar, &stage_tma);
   __syncthreads();
+  if (!staged) {
+    if (threadIdx.x == 0) report(P.status, DEV_STALLED);
+    return;
+  }
   if (lane >= P.lanes) return;
   const int64_t b = ((int64_t)blockIdx.x * warps + warp) * P.lanes + lane;
   if (b >= P.batch) return;
