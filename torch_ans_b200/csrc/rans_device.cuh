@@ -234,7 +234,7 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(unsigned long long* b, uns
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_u32(b)), "r"(bytes) : "memory");
 }
 // global -> shared bulk copy by the copy engine (both addresses 16-byte aligned, size a multiple of
-// 16); its bytes count against the mbarrier's transaction count.  No multicast.
+// 16); its bytes count against the mbarrier's transaction count.  The copy lands in this CTA only.
 __device__ __forceinline__ void bulk_copy_g2s(void* smem, const void* gmem, unsigned bytes, unsigned long long* b) {
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
                    smem_u32(smem)),
