@@ -513,6 +513,101 @@ def test_pop_heavy_tails_and_overrun(C, kernel, layout, lookup, variant, monkeyp
     assert same_rows(st.cpu().numpy(), ref_pop)
 
 
+@pytest.mark.parametrize("lookup", ["search", "invcdf"])
+@pytest.mark.parametrize("variant", VARIANTS)
+def test_bucket_pop_zero_offsets_tails_and_bad_rows(C, lookup, variant, monkeypatch):
+    """The bucket-layout pop with every table offset zero (the kernel then skips the per-step
+    offset read), a table whose last symbol covers whole buckets up to 2^fp, unit-frequency tails
+    (marker buckets), bad indexes and underflow: identical to the oracle.  Then rows whose length
+    points past the row's end (a corrupted length the reference would read past the row for): the
+    bucket pop must agree with the generic pop kernel, which takes the same exact step, and flag
+    underflow."""
+    monkeypatch.setenv("TORCH_ANS_B200_POP_KERNEL", "lean")
+    monkeypatch.setenv("TORCH_ANS_B200_POP_LAYOUT", "bucket_global")
+    rng = np.random.default_rng(zlib.crc32(f"bucket0-{lookup}-{variant}".encode()))
+    fp = FP[variant]
+    fp, cdfs, sizes, _ = _heavy_tail_case(rng, K=5, A=300, fp=fp)
+    # last table: the last symbol takes a large share, so its buckets run up to cum = 2^fp - 1
+    f = np.diff(cdfs[-1].astype(np.int64))
+    f[:] = 1
+    f[-1] += (1 << fp) - f.sum() - 4000
+    f[0] += 4000
+    cdfs[-1] = np.concatenate([[0], np.cumsum(f)]).astype(np.int32)
+    offs = np.zeros(cdfs.shape[0], np.int32)
+    pop_c = np.concatenate([cdfs, O.inverse_quantized_cdf(cdfs, fp)], 1) if lookup == "invcdf" else cdfs
+    K = cdfs.shape[0]
+    B, N, extra = 40, 800, 8
+    idx = rng.integers(0, K, (B, N)).astype(np.int32)
+    sym = rng.integers(0, sizes[idx] - 1).astype(np.int32)
+    last = idx == K - 1
+    sym[last] = np.where(rng.random(last.sum()) < 0.7, sizes[K - 1] - 2, sym[last])
+    ref, perr = O.push(variant, O.init_stream(variant, B), sym, idx, cdfs, sizes, offs, fp, False)
+    assert perr == 0
+    idx_pop = np.concatenate([idx, rng.integers(0, K, (B, extra)).astype(np.int32)], 1)
+    idx_pop[rng.random(idx_pop.shape) < 0.002] = -1
+    ref_pop = ref.copy()
+    dec_ref, derr = O.pop(variant, ref_pop, idx_pop, pop_c, sizes, offs, fp, False, lookup=lookup)
+    assert derr & O.ERR_UNDERFLOW and derr & O.ERR_BAD_INDEX
+    pop = op_names(variant, 1, False, lookup)[1]
+    kw = dict(freq_precision=fp, bypass_coding=False)
+    st = t(ref)
+    dec = getattr(C, pop)(st, t(idx_pop), t(pop_c), t(sizes), t(offs), **kw)
+    assert C.device_status(reset=True) == derr
+    assert np.array_equal(dec.cpu().numpy(), dec_ref)
+    assert same_rows(st.cpu().numpy(), ref_pop)
+    # corrupted lengths: every fourth row claims more bytes than the row holds
+    bad = ref.copy()
+    bad[::4, 0] = (bad.shape[1] - 1) * 4 + 16
+    outs = {}
+    for kernel in ("lean", "generic"):
+        monkeypatch.setenv("TORCH_ANS_B200_POP_KERNEL", kernel)
+        st = t(bad)
+        d = getattr(C, pop)(st, t(idx), t(pop_c), t(sizes), t(offs), **kw)
+        outs[kernel] = (d.cpu().numpy(), st.cpu().numpy(), C.device_status(reset=True))
+    assert outs["lean"][2] == outs["generic"][2] and outs["lean"][2] & O.ERR_UNDERFLOW
+    assert np.array_equal(outs["lean"][0], outs["generic"][0])
+    assert np.array_equal(outs["lean"][1], outs["generic"][1])
+    # the rows with intact lengths decode as before
+    assert np.array_equal(outs["lean"][0][1::4], sym[1::4])
+
+
+@pytest.mark.parametrize("lookup", ["search", "invcdf"])
+@pytest.mark.parametrize("variant", VARIANTS)
+def test_bucket_pop_secondary_table_overflow(C, lookup, variant, monkeypatch):
+    """Tables whose symbols alternate between frequency 1 and 2 over most of the range: nearly half
+    of the buckets hold several symbols that are not a unit run, more than the secondary per-cum
+    table has room for, so some of them decode from secondary blocks and the rest through the
+    exact step.  Both must give the oracle's bytes."""
+    monkeypatch.setenv("TORCH_ANS_B200_POP_KERNEL", "lean")
+    monkeypatch.setenv("TORCH_ANS_B200_POP_LAYOUT", "bucket_global")
+    rng = np.random.default_rng(zlib.crc32(f"secovf-{lookup}-{variant}".encode()))
+    fp = FP[variant]
+    A = 5000 if fp == 15 else 10000
+    rows = []
+    for k in range(2):
+        f = np.where(np.arange(A) % 2 == 0, 1, 2).astype(np.int64)
+        f[rng.integers(0, A)] += (1 << fp) - f.sum()
+        rows.append(np.concatenate([[0], np.cumsum(f)]))
+    cdfs = np.stack(rows).astype(np.int32)
+    sizes = np.full(2, A + 1, np.int32)
+    offs = np.array([0, 3], np.int32)
+    pop_c = np.concatenate([cdfs, O.inverse_quantized_cdf(cdfs, fp)], 1) if lookup == "invcdf" else cdfs
+    B, N = 16, 400
+    idx = rng.integers(0, 2, (B, N)).astype(np.int32)
+    sym = (rng.integers(0, A, (B, N)) + offs[idx]).astype(np.int32)  # uniform: tail symbols everywhere
+    ref, perr = O.push(variant, O.init_stream(variant, B), sym, idx, cdfs, sizes, offs, fp, False)
+    assert perr == 0
+    ref_pop = ref.copy()
+    dec_ref, derr = O.pop(variant, ref_pop, idx, pop_c, sizes, offs, fp, False, lookup=lookup)
+    assert derr == 0
+    pop = op_names(variant, 1, False, lookup)[1]
+    st = t(ref)
+    dec = getattr(C, pop)(st, t(idx), t(pop_c), t(sizes), t(offs), freq_precision=fp, bypass_coding=False)
+    assert C.device_status(reset=True) == 0
+    assert np.array_equal(dec.cpu().numpy(), sym)
+    assert same_rows(st.cpu().numpy(), ref_pop)
+
+
 @pytest.mark.parametrize("case", ["valid", "not_power_of_two", "bad_sum", "oversize", "mixed"])
 def test_alias_build_on_device_matches_host(C, case):
     """rans_alias_build_table on CUDA tables (the device builder, tans_alias_build_table) returns

@@ -78,52 +78,84 @@ __global__ void build_split_s_kernel(const int32_t* cdfs, int64_t ntables, int64
 // Bucket table: one 8-byte entry per 16 consecutive cum values of a table,
 //   bits  0..15  s0, the symbol of the bucket's first cum (0xFFFF: the entry cannot describe the
 //                bucket; those cum values are decoded through the split tables),
-//   bits 16..31  start0, the start of s0 (it may lie before the bucket),
-//   bits 32..47  freq(s0) - 1,
-//   bits 48..63  freq(s0 + 1) - 1 (0 when s0 covers the whole bucket).
-// Decode: c1 = start0 + freq(s0); a cum below c1 is s0 (start0, freq(s0)), a cum at or past c1 is
-// s0 + 1 (start c1, freq(s0 + 1)), so at most one boundary lies inside a bucket.  Every cum of the
-// bucket is checked against the reference lookup when the entry is built.
+//   bits 16..31  c1 - 1, where c1 = start(s0) + freq(s0) is the start of s0 + 1 (it may lie past
+//                the bucket),
+//   bits 32..47  freq(s0),
+//   bits 48..63  freq(s0 + 1) (0 when s0 covers the whole bucket).
+// Decode: a cum below c1 is s0 (start c1 - freq(s0)), a cum at or past c1 is s0 + 1 (start c1), so
+// at most one boundary lies inside a bucket; "cum >= c1" is the single compare
+// (cum << 16) > (bits 0..31).  Every cum of the bucket is checked against the reference lookup when
+// the entry is built.  A bucket with more symbols carries a marker (bits 0..15 = 0xFFFF) whose bits
+// 16..17 say how the rare step decodes it:
+//   0  the exact step (the split tables, or the direct lookup);
+//   1  a run of unit-frequency symbols: symbol = cum + (int32)(bits 32..63), freq 1, offset 0;
+//   2  a block of 16 per-cum entries s | (cum - start) << 16 | freq << 32 in the secondary table,
+//      at block index bits 18..63 (blocks are handed out by an atomic counter up to the table's
+//      capacity; the order differs between builds, the decoded values do not).
+// One extra row (index ntables) holds only type-0 markers: the decoders route table indexes
+// outside the table list to it.
 template <int V, int LK>
 __global__ void build_bucket_kernel(const int32_t* cdfs, int64_t ntables, int64_t cdf_width, const TableInfo* tinfo,
-                                    int fp, unsigned long long* BK) {
-  const int64_t nb = (int64_t)1 << (fp - kBucketBits), total = ntables * nb;
+                                    int fp, unsigned long long* BK, unsigned long long* SEC, int64_t sec_cap,
+                                    unsigned long long* sec_count) {
+  constexpr int NB = 1 << kBucketBits;
+  const int64_t nb = (int64_t)1 << (fp - kBucketBits), total = (ntables + 1) * nb;
   for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
     const int64_t k = e / nb;
+    if (k >= ntables) {
+      BK[e] = 0xFFFFull;
+      continue;
+    }
     const int32_t lo = (int32_t)((e - k * nb) << kBucketBits);
     const TableInfo t = tinfo[k];
     const int32_t* row = cdfs + k * cdf_width;
+    int64_t s[NB];
+    int32_t off[NB], f[NB];
+    bool all = true;
+    for (int i = 0; i < NB; ++i) {
+      all = all && lookup_symbol<V, LK>(row, t, lo + i, cdf_width, fp, s[i], off[i], f[i]);
+      if (!all) break;
+    }
     unsigned long long out = 0xFFFFull;
-    int64_t s0 = 0;
-    int32_t off0 = 0, f0 = 0;
-    bool good = lookup_symbol<V, LK>(row, t, lo, cdf_width, fp, s0, off0, f0);
-    const int32_t start0 = lo - off0;
-    good = good && s0 >= 0 && s0 < 0xFFFE && start0 >= 0 && start0 <= 0xFFFF && f0 >= 1 && f0 <= 0x10000;
-    const int32_t c1 = start0 + f0;
-    int32_t f1 = 1;
-    bool seen1 = false;
-    for (int i = 1; good && i < (1 << kBucketBits); ++i) {
-      int64_t s;
-      int32_t off, f;
-      const int32_t cum = lo + i;
-      if (!lookup_symbol<V, LK>(row, t, cum, cdf_width, fp, s, off, f)) {
-        good = false;
-        break;
-      }
-      const int32_t st = cum - off;
-      if (cum < c1) {
-        good = s == s0 && st == start0 && f == f0;
-      } else {
-        if (!seen1) {
-          f1 = f;
-          seen1 = true;
+    if (all) {
+      const int64_t s0 = s[0];
+      const int32_t start0 = lo - off[0], f0 = f[0];
+      const int32_t c1 = start0 + f0;
+      bool good = s0 >= 0 && s0 < 0xFFFE && start0 >= 0 && start0 <= 0xFFFF && f0 >= 1 && f0 <= 0xFFFF;
+      int32_t f1 = 1;
+      bool seen1 = false;
+      bool unit = true, packs = true;
+      for (int i = 0; i < NB; ++i) {
+        const int32_t cum = lo + i, st = cum - off[i];
+        if (i > 0 && good) {
+          if (cum < c1) {
+            good = s[i] == s0 && st == start0 && f[i] == f0;
+          } else {
+            if (!seen1) {
+              f1 = f[i];
+              seen1 = true;
+            }
+            good = s[i] == s0 + 1 && st == c1 && f[i] == f1 && f1 >= 1 && f1 <= 0xFFFF;
+          }
         }
-        good = s == s0 + 1 && st == c1 && f == f1 && f1 >= 1 && f1 <= 0x10000;
+        unit = unit && f[i] == 1 && off[i] == 0 && s[i] == s0 + i;
+        packs = packs && s[i] >= 0 && s[i] < 0xFFFF && off[i] >= 0 && off[i] <= 0xFFFF && f[i] >= 1 && f[i] <= 0x10000;
+      }
+      if (good) {
+        out = (unsigned long long)s0 | ((unsigned long long)(c1 - 1) << 16) | ((unsigned long long)f0 << 32) |
+              ((unsigned long long)(seen1 ? f1 : 0) << 48);
+      } else if (unit && s0 - lo >= INT32_MIN && s0 - lo <= INT32_MAX) {
+        out = 0xFFFFull | (1ull << 16) | ((unsigned long long)(uint32_t)(int32_t)(s0 - lo) << 32);
+      } else if (packs && sec_cap > 0) {
+        const unsigned long long blk = atomicAdd(sec_count, 1ull);
+        if (blk < (unsigned long long)sec_cap) {
+          for (int i = 0; i < NB; ++i)
+            SEC[blk * NB + i] = (unsigned long long)s[i] | ((unsigned long long)off[i] << 16) |
+                                ((unsigned long long)f[i] << 32);
+          out = 0xFFFFull | (2ull << 16) | (blk << 18);
+        }
       }
     }
-    if (good)
-      out = (unsigned long long)s0 | ((unsigned long long)start0 << 16) | ((unsigned long long)(f0 - 1) << 32) |
-            ((unsigned long long)(f1 - 1) << 48);
     BK[e] = out;
   }
 }
@@ -363,7 +395,19 @@ static int64_t split_bytes(int lookup, int64_t ntables, int64_t cdf_width, int f
   return ntables * ((int64_t)2 << fp) + ntables * split_stride(lookup, cdf_width, fp) * 4;
 }
 
-static int64_t bucket_bytes(int64_t ntables, int fp) { return fp >= kBucketBits ? ntables * ((int64_t)8 << (fp - kBucketBits)) : 0; }
+// bucket table: ntables + 1 rows (the last one all markers) of 2^(fp-1) bytes, the first row
+// aligned to a row's size (so a row address plus an offset inside the row needs no carry); then a
+// 256-byte counter slot and the secondary table of per-cum blocks (128 bytes each) for marker
+// buckets, with room for one bucket in 16
+static int64_t bucket_row_bytes(int fp) { return (int64_t)8 << (fp - kBucketBits); }
+static int64_t bucket_sec_cap(int64_t ntables, int fp) {
+  return std::max<int64_t>(64, (ntables << (fp - kBucketBits)) / 16);
+}
+static int64_t bucket_bytes(int64_t ntables, int fp) {
+  return fp >= kBucketBits
+             ? (ntables + 2) * bucket_row_bytes(fp) + 256 + bucket_sec_cap(ntables, fp) * (8 << kBucketBits)
+             : 0;
+}
 
 static bool tables_enabled() {
   const char* e = std::getenv("TORCH_ANS_B200_FUSED");
@@ -648,7 +692,13 @@ int pop_impl(int variant, int lookup, int interleave, int32_t* stream, int64_t b
     wsp += align_up((size_t)(ntables << fp) * 2);
     P.fST = reinterpret_cast<uint32_t*>(wsp);
     wsp += align_up((size_t)ntables * sstride * 4);
-    if (need_bucket) P.fBK = reinterpret_cast<unsigned long long*>(wsp);
+    if (need_bucket) {
+      const uintptr_t rb = (uintptr_t)bucket_row_bytes(fp);
+      P.fBK = reinterpret_cast<unsigned long long*>((reinterpret_cast<uintptr_t>(wsp) + rb - 1) & ~(rb - 1));
+      char* after = reinterpret_cast<char*>(const_cast<unsigned long long*>(P.fBK)) + (ntables + 1) * rb;
+      P.fSEC = reinterpret_cast<unsigned long long*>(after + 256);
+      P.sec_cap = bucket_sec_cap(ntables, fp);
+    }
   }
   {
     const int blocks = (int)std::min<int64_t>((ntables + 255) / 256, 4 * (int64_t)dev_sms);
@@ -665,17 +715,21 @@ int pop_impl(int variant, int lookup, int interleave, int32_t* stream, int64_t b
   }
   if (need_bucket) {
     unsigned long long* BK = const_cast<unsigned long long*>(P.fBK);
-    const int64_t nbk = ntables << (fp - kBucketBits);
+    unsigned long long* SEC = const_cast<unsigned long long*>(P.fSEC);
+    unsigned long long* cnt = SEC - 32;  // the counter slot before the secondary table
+    // without a zeroed counter no secondary blocks are handed out (type-2 buckets stay type 0)
+    const int64_t sc = cudaMemsetAsync(cnt, 0, sizeof(unsigned long long), s) == cudaSuccess ? P.sec_cap : 0;
+    const int64_t nbk = (ntables + 1) << (fp - kBucketBits);
     const int bb = (int)std::max<int64_t>(1, std::min<int64_t>((nbk + 127) / 128, 16 * (int64_t)dev_sms));
     note_launch();
     if (lookup == TANS_LOOKUP_INVCDF) {
-      if (variant == TANS_RANS64) build_bucket_kernel<0, LK_INVCDF><<<bb, 128, 0, s>>>(cdfs, ntables, cdf_width, tinfo, fp, BK);
-      else if (variant == TANS_RANS32) build_bucket_kernel<1, LK_INVCDF><<<bb, 128, 0, s>>>(cdfs, ntables, cdf_width, tinfo, fp, BK);
-      else build_bucket_kernel<2, LK_INVCDF><<<bb, 128, 0, s>>>(cdfs, ntables, cdf_width, tinfo, fp, BK);
+      if (variant == TANS_RANS64) build_bucket_kernel<0, LK_INVCDF><<<bb, 128, 0, s>>>(cdfs, ntables, cdf_width, tinfo, fp, BK, SEC, sc, cnt);
+      else if (variant == TANS_RANS32) build_bucket_kernel<1, LK_INVCDF><<<bb, 128, 0, s>>>(cdfs, ntables, cdf_width, tinfo, fp, BK, SEC, sc, cnt);
+      else build_bucket_kernel<2, LK_INVCDF><<<bb, 128, 0, s>>>(cdfs, ntables, cdf_width, tinfo, fp, BK, SEC, sc, cnt);
     } else {
-      if (variant == TANS_RANS64) build_bucket_kernel<0, LK_SEARCH><<<bb, 128, 0, s>>>(cdfs, ntables, cdf_width, tinfo, fp, BK);
-      else if (variant == TANS_RANS32) build_bucket_kernel<1, LK_SEARCH><<<bb, 128, 0, s>>>(cdfs, ntables, cdf_width, tinfo, fp, BK);
-      else build_bucket_kernel<2, LK_SEARCH><<<bb, 128, 0, s>>>(cdfs, ntables, cdf_width, tinfo, fp, BK);
+      if (variant == TANS_RANS64) build_bucket_kernel<0, LK_SEARCH><<<bb, 128, 0, s>>>(cdfs, ntables, cdf_width, tinfo, fp, BK, SEC, sc, cnt);
+      else if (variant == TANS_RANS32) build_bucket_kernel<1, LK_SEARCH><<<bb, 128, 0, s>>>(cdfs, ntables, cdf_width, tinfo, fp, BK, SEC, sc, cnt);
+      else build_bucket_kernel<2, LK_SEARCH><<<bb, 128, 0, s>>>(cdfs, ntables, cdf_width, tinfo, fp, BK, SEC, sc, cnt);
     }
   }
   if (fast) {

@@ -28,6 +28,8 @@ struct PopParams {
   const uint32_t* fST; // split layout: per-symbol {freq - 1, start} ST[k][s]
   int64_t st_stride;   // split layout: entries per table in ST
   const unsigned long long* fBK;  // bucket layout: one entry per 16 cum values
+  const unsigned long long* fSEC; // bucket layout: per-cum blocks of marker buckets (type 2)
+  int64_t sec_cap;                // blocks the secondary table holds
   int spt;             // streams per thread (fast kernel)
   int fused_smem;      // fused table staged in shared memory
   int tin_smem;        // per-table info staged in shared memory

@@ -12,7 +12,7 @@
 //   TM_FUSED_SMEM / TM_FUSED_GLOBAL: D[k][cum] = (freq - 1) | (cum - start) << 16, S[k][cum] = s
 //   TM_SPLIT_SMEM / TM_SPLIT_GLOBAL: S[k][cum] = s, ST[k][s] = (freq - 1) | start << 16
 //   TM_BUCKET_GLOBAL: one 8-byte entry per 16 cum values holding the bucket's first symbol, its
-//     start and freq and the freq of the next symbol (so at most one boundary inside the bucket):
+//     freq, the start and freq of the next symbol (so at most one boundary inside the bucket):
 //     one load resolves (s, start, freq); buckets the entry cannot describe (verified per cum at
 //     build time) carry a marker and use the split tables, which are built alongside
 // S = 0xFFFF marks the entries the packed layouts cannot hold; those steps take the direct lookup.
@@ -318,15 +318,15 @@ __global__ void __launch_bounds__(512) pop_fast_kernel(const PopParams P) {
           bool fb_any = false;
 #pragma unroll
           for (int j = 0; j < SPT; ++j) {
+            // lo = s0 | (c1 - 1) << 16, hi = freq(s0) | freq(s0 + 1) << 16
             const uint32_t lo = (uint32_t)bk[j], hi = (uint32_t)(bk[j] >> 32);
-            const uint32_t s0 = lo & 0xFFFFu, start0 = lo >> 16;
+            const uint32_t s0 = lo & 0xFFFFu, c1 = (lo >> 16) + 1u, f0 = hi & 0xFFFFu;
             fb[j] = s0 == 0xFFFFu;
             fb_any |= fb[j];
-            const uint32_t c1 = start0 + (hi & 0xFFFFu) + 1u;
-            const bool up = cum[j] >= c1;
+            const bool up = (cum[j] << 16) > lo;  // cum >= c1
             sv[j] = s0 + (up ? 1u : 0u);
             // d = (freq - 1) | start << 16 (start < 2^16 for every describable bucket)
-            d[j] = up ? ((hi >> 16) | (c1 << 16)) : ((hi & 0xFFFFu) | (start0 << 16));
+            d[j] = up ? (((hi >> 16) - 1u) | (c1 << 16)) : ((f0 - 1u) | ((c1 - f0) << 16));
           }
           if (__any_sync(__activemask(), fb_any)) {
 #pragma unroll

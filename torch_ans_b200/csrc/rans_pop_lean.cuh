@@ -140,18 +140,7 @@ __global__ void __launch_bounds__(512) pop_lean_kernel(const PopParams P) {
       const uint32_t cum = (uint32_t)x & cmask;
       uint32_t sv, fm1, off;
       bool slow = row_bad || (uint32_t)k > kmax;
-      if constexpr (TM == TM_BUCKET_GLOBAL) {
-        const unsigned long long bk =
-            ld_hint_u64(P.fBK + (((size_t)kc << (P.fp - kBucketBits)) + (cum >> kBucketBits)), pol_keep);
-        const uint32_t lo = (uint32_t)bk, hi = (uint32_t)(bk >> 32);
-        const uint32_t s0 = lo & 0xFFFFu, start0 = lo >> 16;
-        const uint32_t c1 = start0 + (hi & 0xFFFFu) + 1u;
-        const bool up = cum >= c1;
-        slow |= s0 == 0xFFFFu;
-        sv = s0 + (up ? 1u : 0u);
-        fm1 = up ? (hi >> 16) : (hi & 0xFFFFu);
-        off = cum - (up ? c1 : start0);
-      } else if constexpr (TM == TM_FUSED_SMEM || TM == TM_FUSED_GLOBAL) {
+      if constexpr (TM == TM_FUSED_SMEM || TM == TM_FUSED_GLOBAL) {
         const size_t e = ((size_t)kc << P.fp) | cum;
         uint32_t d;
         if constexpr (TM == TM_FUSED_SMEM) {
@@ -221,9 +210,259 @@ __global__ void __launch_bounds__(512) pop_lean_kernel(const PopParams P) {
   report(P.status, err);
 }
 
+// The rare step of the bucket pop, out of line with the state passed by value: marker entries of
+// type 1 (unit-frequency run: symbol = cum + d, freq 1, offset 0) and type 2 (one load from the
+// secondary table's per-cum block) decode here with the same update and refill as the straight
+// step; everything else (type-0 markers, bad indexes, escapes) takes the exact step.
+template <int V, int LK, bool BYPASS>
+__device__ __noinline__ LeanState<V> popb_rare(const PopParams P, LeanState<V> st, const int32_t* row, int32_t k,
+                                               unsigned long long e, const TableInfo* tsm) {
+  using S = typename VT<V>::State;
+  const uint32_t kind = (uint32_t)(e >> 16) & 3u;
+  if ((e & 0xFFFFull) == 0xFFFFull && (kind == 1u || kind == 2u) && (uint32_t)k < (uint64_t)P.ntables) {
+    const uint32_t cum = (uint32_t)st.x & ((1u << P.fp) - 1u);
+    uint32_t f, off;
+    int32_t sv;
+    if (kind == 1u) {
+      f = 1u;
+      off = 0u;
+      sv = (int32_t)(cum + (uint32_t)(e >> 32));
+    } else {
+      const unsigned long long d =
+          ld_hint_u64(P.fSEC + ((e >> 18) << kBucketBits) + (cum & ((1u << kBucketBits) - 1u)), policy_evict_last());
+      sv = (int32_t)(d & 0xFFFFull);
+      off = (uint32_t)(d >> 16) & 0xFFFFu;
+      f = (uint32_t)(d >> 32);
+    }
+    const TableInfo ti = tsm[k];
+    if (!BYPASS || sv != ti.size - 2) {
+      FastCursor<V> cur;
+      cur.c.payload = reinterpret_cast<const uint8_t*>(row + 1);
+      cur.c.p = st.p;
+      cur.c.first = VT<V>::SBYTES / VT<V>::WBYTES;
+      cur.c.cap = (P.width - 1) * 4 / VT<V>::WBYTES;
+      cur.c.err = st.err;
+      cur.nextw = st.nextw;
+      S x = st.x;
+      x = (S)((x >> P.fp) * (S)f + (S)off);
+      cur.refill(x);
+      if constexpr (VT<V>::LOOP) cur.prime();
+      st.x = x;
+      st.nextw = cur.nextw;
+      st.p = cur.c.p;
+      st.err = cur.c.err;
+      st.v = (int32_t)((uint32_t)sv + (uint32_t)ti.offset);
+      return st;
+    }
+  }
+  return popl_exact<V, LK, BYPASS, TM_BUCKET_GLOBAL>(P, st, row, k, tsm, nullptr, nullptr);
+}
+
+// Stream word at p when `pred`, else `w` (a predicated load, zero-extended: no branch on the
+// serial step)
+__device__ __forceinline__ uint32_t ld_word_if(const uint32_t* p, bool pred, uint32_t w) {
+  asm("{\n .reg .pred q;\n setp.ne.u32 q, %2, 0;\n @q ld.global.nc.u32 %0, [%1];\n}\n"
+      : "+r"(w)
+      : "l"(p), "r"((uint32_t)pred));
+  return w;
+}
+__device__ __forceinline__ uint32_t ld_word_if(const uint16_t* p, bool pred, uint32_t w) {
+  asm("{\n .reg .pred q;\n setp.ne.u32 q, %2, 0;\n @q ld.global.nc.u16 %0, [%1];\n}\n"
+      : "+r"(w)
+      : "l"(p), "r"((uint32_t)pred));
+  return w;
+}
+__device__ __forceinline__ uint32_t ld_word_if(const uint8_t* p, bool pred, uint32_t w) {
+  asm("{\n .reg .pred q;\n setp.ne.u32 q, %2, 0;\n @q ld.global.nc.u8 %0, [%1];\n}\n"
+      : "+r"(w)
+      : "l"(p), "r"((uint32_t)pred));
+  return w;
+}
+
+// Pop over the bucket layout (TM_BUCKET_GLOBAL): one dependent L2 load per step.
+//
+// Entry of 16 cum values (built per call, every cum checked against the reference lookup):
+//   lo = s0 | (c1 - 1) << 16,  hi = f0 | f1 << 16
+// (s0 the symbol of the bucket's first cum, f0 its freq, c1 the start of s0 + 1, f1 its freq;
+// s0 = 0xFFFF marks a bucket the entry cannot describe, which the out-of-line rare step decodes:
+// unit-frequency runs with no load, other buckets from a per-cum block in one more load, the
+// remaining cases by the exact step).  The serial chain of a step is
+//   entry load -> up = (cum << 16) > lo, one compare on the loaded word -> freq = up ? f1 : f0,
+//   offset = cum - c1 + (up ? 0 : f0) -> x = freq * (x >> fp) + offset -> refill test ->
+//   next entry address,
+// where the next address is a select between the two candidates computed beside the refill test
+// (refill: the low word becomes the prefetched stream word; else the low word of the product),
+// each a row address OR-ed with (low word >> 1) & mask: rows are aligned to their size, so the OR
+// is the add.  A row of markers after the last table stands for table indexes outside the table
+// list, so the marker test is the step's only check.  Off the chain: symbol output and table
+// offsets (read only when some table has a non-zero offset, or for the escape slot), index loads
+// two chunks ahead in a fixed ring of registers, the predicated prefetch of the next stream word,
+// and the underflow test, made once at the end of the stream (a refill read below the first data
+// word happened exactly when the cursor fell below first - 1).
+template <int V, int LK, bool BYPASS>
+__global__ void __maxnreg__(96) pop_bucket_kernel(const PopParams P) {
+  using S = typename VT<V>::State;
+  using W = typename VT<V>::Word;
+  constexpr int TM = TM_BUCKET_GLOBAL;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  const int T = blockDim.x, tid = threadIdx.x;
+  const int warps = T >> 5, warp = tid >> 5, lane = tid & 31;
+  // per-table records: TableInfo, then {offset, escape slot} with one more entry for the marker
+  // row (the shared region holds 32 bytes per table, these use 24 + 8)
+  TableInfo* tsm = reinterpret_cast<TableInfo*>(smem_raw);
+  int2* tsm2 = reinterpret_cast<int2*>(tsm + P.ntables);
+  int any_off = 0;
+  for (int64_t k = tid; k < P.ntables; k += T) {
+    const TableInfo ti = P.tinfo[k];
+    tsm[k] = ti;
+    tsm2[k] = make_int2(ti.offset, BYPASS ? ti.size - 2 : -1);
+    any_off |= ti.offset != 0 ? 1 : 0;
+  }
+  if (tid == 0) tsm2[P.ntables] = make_int2(0, -1);
+  const bool use_off = __syncthreads_or(any_off) != 0;
+  if (lane >= P.lanes) return;
+  const int64_t b = ((int64_t)blockIdx.x * warps + warp) * P.lanes + lane;
+  if (b >= P.batch) return;
+
+  int32_t* row = P.stream + b * P.width;
+  FastCursor<V> cur;
+  cur.c.payload = reinterpret_cast<const uint8_t*>(row + 1);
+  cur.c.p = (int64_t)row[0] / VT<V>::WBYTES - 1;
+  cur.c.first = VT<V>::SBYTES / VT<V>::WBYTES;
+  cur.c.cap = (P.width - 1) * 4 / VT<V>::WBYTES;
+  cur.c.err = 0;
+  S x = load_state<V>(row, 0);
+  cur.prime();
+  const W* pw = reinterpret_cast<const W*>(cur.c.payload);
+  // a row whose length points past its end, or past what 32-bit cursors hold, is decoded exactly
+  const bool row_bad = cur.c.p >= cur.c.cap || cur.c.p > 0x7ffffff0;
+  const int first = (int)cur.c.first;
+  int p = (int)min(max(cur.c.p, (int64_t)-0x7fffffff), (int64_t)0x7fffffff);
+  const int p_init = p;
+  S nextw = cur.nextw;
+  uint32_t err = 0;
+
+  const unsigned long long pol_keep = policy_evict_last(), pol_stream = policy_evict_first();
+  const uint32_t cmask = (1u << P.fp) - 1u;
+  const uint32_t bmask = (cmask >> 1) & ~7u;  // byte offset of cum's entry in its row, from (cum >> 1)
+  const uint32_t kmark = (uint32_t)P.ntables;
+  const int rsh = P.fp - 1;  // log2 of a row's bytes
+  const uintptr_t bk0 = reinterpret_cast<uintptr_t>(P.fBK);
+  const int64_t N = P.nsym;
+  const int nch = (int)(N >> 2);
+  const int32_t* irow = P.idx + b * N;
+  int32_t* orow = P.out + b * N;
+
+  if (row_bad) {
+#pragma unroll 1
+    for (int c = 0; c < nch; ++c) {
+      int32_t ov[4];
+#pragma unroll 1
+      for (int q = 0; q < 4; ++q) {
+        LeanState<V> st{x, nextw, (long long)p, err, 0};
+        st = popl_exact<V, LK, BYPASS, TM>(P, st, row, irow[4 * (int64_t)c + q], tsm, nullptr, nullptr);
+        x = st.x;
+        nextw = st.nextw;
+        p = (int)min(max(st.p, -0x7fffffffll), 0x7fffffffll);
+        err = st.err;
+        ov[q] = st.v;
+      }
+      st_hint_v4(reinterpret_cast<int4*>(orow + 4 * (int64_t)c), make_int4(ov[0], ov[1], ov[2], ov[3]), pol_stream);
+    }
+  } else {
+    // index ring: slot j holds the indexes of the chunk c with c % 2 == j, loaded two chunks
+    // (eight steps) ahead
+    int4 kr[2];
+#pragma unroll
+    for (int j = 0; j < 2; ++j) kr[j] = j < nch ? ld_idx4(irow + 4 * j, pol_stream) : make_int4(0, 0, 0, 0);
+    uintptr_t a = (bk0 + ((uintptr_t)min((uint32_t)kr[0].x, kmark) << rsh)) | ((((uint32_t)x) >> 1) & bmask);
+#pragma unroll 1
+    for (int c0 = 0; c0 < nch; c0 += 2) {
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int c = c0 + j;
+        if (c >= nch) break;
+        const int4 k4 = kr[j];
+        const int32_t knext = kr[j ^ 1].x;  // first index of chunk c + 1
+        if (c + 2 < nch) kr[j] = ld_idx4(irow + 4 * (int64_t)(c + 2), pol_stream);
+        const int32_t kv[5] = {k4.x, k4.y, k4.z, k4.w, knext};
+        int32_t ov[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int32_t k = kv[q];
+          const uintptr_t rown = bk0 + ((uintptr_t)min((uint32_t)kv[q + 1], kmark) << rsh);
+          const S x0 = x, w0 = nextw;
+          const int p0 = p;
+          const unsigned long long e = ld_hint_u64(reinterpret_cast<const unsigned long long*>(a), pol_keep);
+          const uint32_t cum = (uint32_t)x & cmask;
+          const S xs = x >> P.fp;
+          const uint32_t lo = (uint32_t)e, hi = (uint32_t)(e >> 32);
+          const bool up = (cum << 16) > lo;  // cum >= c1
+          const uint32_t f0 = hi & 0xFFFFu;
+          const uint32_t f = up ? (hi >> 16) : f0;
+          const uint32_t off = (cum - 1u - (lo >> 16)) + (up ? 0u : f0);
+          const uint32_t s0 = lo & 0xFFFFu;
+          const uint32_t sv = s0 + (up ? 1u : 0u);
+          int2 om = make_int2(0, -1);
+          if (BYPASS || use_off) om = tsm2[min((uint32_t)k, kmark)];
+          bool slow = s0 == 0xFFFFu;
+          if constexpr (BYPASS) slow |= (int32_t)sv == om.y;
+          x = (S)(xs * (S)f + (S)off);
+          if constexpr (!VT<V>::LOOP) {
+            // single refill (rans64, rans32_16): the low word after a refill is the prefetched word
+            const bool r = (unsigned long long)x < VT<V>::LB;
+            const uintptr_t an = rown | ((((uint32_t)x) >> 1) & bmask);
+            const uintptr_t ar = rown | ((((uint32_t)nextw) >> 1) & bmask);
+            x = r ? (S)((x << VT<V>::WB) | nextw) : x;
+            a = r ? ar : an;
+            p -= r ? 1 : 0;
+            nextw = (S)ld_word_if(pw + p, r && !slow && p >= first, r ? 0u : (uint32_t)nextw);
+          } else {
+            // rans32 (byte words): up to MAX_RENORM refills, the first from the prefetched word
+#pragma unroll
+            for (int t = 0; t < VT<V>::MAX_RENORM; ++t) {
+              const bool r = (unsigned long long)x < VT<V>::LB;
+              x = r ? (S)((x << VT<V>::WB) | nextw) : x;
+              p -= r ? 1 : 0;
+              nextw = (S)ld_word_if(pw + p, r && !slow && p >= first, r ? 0u : (uint32_t)nextw);
+            }
+            a = rown | ((((uint32_t)x) >> 1) & bmask);
+          }
+          ov[q] = (int32_t)(sv + (uint32_t)om.x);
+          // the fast step above is computed before the branch, so the branch is off its chain
+          asm volatile("" ::"l"((unsigned long long)a), "l"((unsigned long long)x));
+          if (slow) {
+            LeanState<V> st{x0, w0, (long long)p0, err, 0};
+            st = popb_rare<V, LK, BYPASS>(P, st, row, k, e, tsm);
+            x = st.x;
+            nextw = st.nextw;
+            p = (int)min(max(st.p, -0x7fffffffll), 0x7fffffffll);
+            err = st.err;
+            ov[q] = st.v;
+            a = rown | ((((uint32_t)x) >> 1) & bmask);
+          }
+        }
+        st_hint_v4(reinterpret_cast<int4*>(orow + 4 * (int64_t)c), make_int4(ov[0], ov[1], ov[2], ov[3]), pol_stream);
+      }
+    }
+    if (p < p_init && p + 1 < first) err |= DEV_UNDERFLOW;
+  }
+  store_state<V>(row, 0, x);
+  row[0] = (int32_t)(((int64_t)p + 1) * VT<V>::WBYTES);
+  report(P.status, err);
+}
+
 template <int V>
 bool launch_pop_lean(const PopParams& P, int lookup, bool bypass, int tm, int blocks, int threads, size_t smem,
                      cudaStream_t s);
+
+template <int V, int LK, bool BY>
+void popb_go(const PopParams& P, int blocks, int threads, size_t smem, cudaStream_t s) {
+  if (smem > 48 * 1024)
+    cudaFuncSetAttribute(pop_bucket_kernel<V, LK, BY>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  pop_bucket_kernel<V, LK, BY><<<blocks, threads, smem, s>>>(P);
+  note_launch();
+}
 
 template <int V, int LK, bool BY, int TM>
 void popl_go(const PopParams& P, int blocks, int threads, size_t smem, cudaStream_t s) {
@@ -242,14 +481,14 @@ bool popl_tm(const PopParams& P, int lookup, int tm, int blocks, int threads, si
     return true;
   }
   if (lookup == 1) {
-    if (tm == TM_BUCKET_GLOBAL) popl_go<V, 1, BY, TM_BUCKET_GLOBAL>(P, blocks, threads, smem, s);
+    if (tm == TM_BUCKET_GLOBAL) popb_go<V, 1, BY>(P, blocks, threads, smem, s);
     else if (tm == TM_FUSED_SMEM) popl_go<V, 1, BY, TM_FUSED_SMEM>(P, blocks, threads, smem, s);
     else if (tm == TM_SPLIT_SMEM) popl_go<V, 1, BY, TM_SPLIT_SMEM>(P, blocks, threads, smem, s);
     else if (tm == TM_SPLIT_GLOBAL) popl_go<V, 1, BY, TM_SPLIT_GLOBAL>(P, blocks, threads, smem, s);
     else return false;
     return true;
   }
-  if (tm == TM_BUCKET_GLOBAL) popl_go<V, 0, BY, TM_BUCKET_GLOBAL>(P, blocks, threads, smem, s);
+  if (tm == TM_BUCKET_GLOBAL) popb_go<V, 0, BY>(P, blocks, threads, smem, s);
   else if (tm == TM_FUSED_SMEM) popl_go<V, 0, BY, TM_FUSED_SMEM>(P, blocks, threads, smem, s);
   else if (tm == TM_SPLIT_SMEM) popl_go<V, 0, BY, TM_SPLIT_SMEM>(P, blocks, threads, smem, s);
   else if (tm == TM_SPLIT_GLOBAL) popl_go<V, 0, BY, TM_SPLIT_GLOBAL>(P, blocks, threads, smem, s);
