@@ -339,14 +339,14 @@ __global__ void __maxnreg__(96) pop_bucket_kernel(const PopParams P) {
   const int first = (int)cur.c.first;
   int p = (int)min(max(cur.c.p, (int64_t)-0x7fffffff), (int64_t)0x7fffffff);
   const int p_init = p;
-  S nextw = cur.nextw;
+  uint32_t nextw = (uint32_t)cur.nextw;  // every word type fits 32 bits
   uint32_t err = 0;
 
   const unsigned long long pol_keep = policy_evict_last(), pol_stream = policy_evict_first();
   const uint32_t cmask = (1u << P.fp) - 1u;
   const uint32_t bmask = (cmask >> 1) & ~7u;  // byte offset of cum's entry in its row, from (cum >> 1)
   const uint32_t kmark = (uint32_t)P.ntables;
-  const int rsh = P.fp - 1;  // log2 of a row's bytes
+  const uint32_t rowbytes = 1u << (P.fp - 1);
   const uintptr_t bk0 = reinterpret_cast<uintptr_t>(P.fBK);
   const int64_t N = P.nsym;
   const int nch = (int)(N >> 2);
@@ -359,10 +359,10 @@ __global__ void __maxnreg__(96) pop_bucket_kernel(const PopParams P) {
       int32_t ov[4];
 #pragma unroll 1
       for (int q = 0; q < 4; ++q) {
-        LeanState<V> st{x, nextw, (long long)p, err, 0};
+        LeanState<V> st{x, (S)nextw, (long long)p, err, 0};
         st = popl_exact<V, LK, BYPASS, TM>(P, st, row, irow[4 * (int64_t)c + q], tsm, nullptr, nullptr);
         x = st.x;
-        nextw = st.nextw;
+        nextw = (uint32_t)st.nextw;
         p = (int)min(max(st.p, -0x7fffffffll), 0x7fffffffll);
         err = st.err;
         ov[q] = st.v;
@@ -375,7 +375,7 @@ __global__ void __maxnreg__(96) pop_bucket_kernel(const PopParams P) {
     int4 kr[2];
 #pragma unroll
     for (int j = 0; j < 2; ++j) kr[j] = j < nch ? ld_idx4(irow + 4 * j, pol_stream) : make_int4(0, 0, 0, 0);
-    uintptr_t a = (bk0 + ((uintptr_t)min((uint32_t)kr[0].x, kmark) << rsh)) | ((((uint32_t)x) >> 1) & bmask);
+    uintptr_t a = (bk0 + (uintptr_t)min((uint32_t)kr[0].x, kmark) * rowbytes) | ((((uint32_t)x) >> 1) & bmask);
 #pragma unroll 1
     for (int c0 = 0; c0 < nch; c0 += 2) {
 #pragma unroll
@@ -386,12 +386,24 @@ __global__ void __maxnreg__(96) pop_bucket_kernel(const PopParams P) {
         const int32_t knext = kr[j ^ 1].x;  // first index of chunk c + 1
         if (c + 2 < nch) kr[j] = ld_idx4(irow + 4 * (int64_t)(c + 2), pol_stream);
         const int32_t kv[5] = {k4.x, k4.y, k4.z, k4.w, knext};
+        // table offsets (and escape slots) of the chunk's four steps, read only when some table
+        // has an offset or escapes are coded (a block-uniform branch, once per chunk)
+        int32_t ofs[4] = {0, 0, 0, 0}, esc[4] = {-1, -1, -1, -1};
+        if (BYPASS || use_off) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int2 om = tsm2[min((uint32_t)kv[q], kmark)];
+            ofs[q] = om.x;
+            esc[q] = om.y;
+          }
+        }
         int32_t ov[4];
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
           const int32_t k = kv[q];
-          const uintptr_t rown = bk0 + ((uintptr_t)min((uint32_t)kv[q + 1], kmark) << rsh);
-          const S x0 = x, w0 = nextw;
+          const uintptr_t rown = bk0 + (uintptr_t)min((uint32_t)kv[q + 1], kmark) * rowbytes;
+          const S x0 = x;
+          const uint32_t w0 = nextw;
           const int p0 = p;
           const unsigned long long e = ld_hint_u64(reinterpret_cast<const unsigned long long*>(a), pol_keep);
           const uint32_t cum = (uint32_t)x & cmask;
@@ -403,39 +415,37 @@ __global__ void __maxnreg__(96) pop_bucket_kernel(const PopParams P) {
           const uint32_t off = (cum - 1u - (lo >> 16)) + (up ? 0u : f0);
           const uint32_t s0 = lo & 0xFFFFu;
           const uint32_t sv = s0 + (up ? 1u : 0u);
-          int2 om = make_int2(0, -1);
-          if (BYPASS || use_off) om = tsm2[min((uint32_t)k, kmark)];
           bool slow = s0 == 0xFFFFu;
-          if constexpr (BYPASS) slow |= (int32_t)sv == om.y;
+          if constexpr (BYPASS) slow |= (int32_t)sv == esc[q];
           x = (S)(xs * (S)f + (S)off);
           if constexpr (!VT<V>::LOOP) {
             // single refill (rans64, rans32_16): the low word after a refill is the prefetched word
             const bool r = (unsigned long long)x < VT<V>::LB;
             const uintptr_t an = rown | ((((uint32_t)x) >> 1) & bmask);
-            const uintptr_t ar = rown | ((((uint32_t)nextw) >> 1) & bmask);
-            x = r ? (S)((x << VT<V>::WB) | nextw) : x;
+            const uintptr_t ar = rown | ((nextw >> 1) & bmask);
+            x = r ? (S)((x << VT<V>::WB) | (S)nextw) : x;
             a = r ? ar : an;
             p -= r ? 1 : 0;
-            nextw = (S)ld_word_if(pw + p, r && !slow && p >= first, r ? 0u : (uint32_t)nextw);
+            nextw = ld_word_if(pw + p, r && !slow && p >= first, r ? 0u : nextw);
           } else {
             // rans32 (byte words): up to MAX_RENORM refills, the first from the prefetched word
 #pragma unroll
             for (int t = 0; t < VT<V>::MAX_RENORM; ++t) {
               const bool r = (unsigned long long)x < VT<V>::LB;
-              x = r ? (S)((x << VT<V>::WB) | nextw) : x;
+              x = r ? (S)((x << VT<V>::WB) | (S)nextw) : x;
               p -= r ? 1 : 0;
-              nextw = (S)ld_word_if(pw + p, r && !slow && p >= first, r ? 0u : (uint32_t)nextw);
+              nextw = ld_word_if(pw + p, r && !slow && p >= first, r ? 0u : nextw);
             }
             a = rown | ((((uint32_t)x) >> 1) & bmask);
           }
-          ov[q] = (int32_t)(sv + (uint32_t)om.x);
+          ov[q] = (int32_t)(sv + (uint32_t)ofs[q]);
           // the fast step above is computed before the branch, so the branch is off its chain
           asm volatile("" ::"l"((unsigned long long)a), "l"((unsigned long long)x));
           if (slow) {
-            LeanState<V> st{x0, w0, (long long)p0, err, 0};
+            LeanState<V> st{x0, (S)w0, (long long)p0, err, 0};
             st = popb_rare<V, LK, BYPASS>(P, st, row, k, e, tsm);
             x = st.x;
-            nextw = st.nextw;
+            nextw = (uint32_t)st.nextw;
             p = (int)min(max(st.p, -0x7fffffffll), 0x7fffffffll);
             err = st.err;
             ov[q] = st.v;
