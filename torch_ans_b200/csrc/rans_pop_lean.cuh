@@ -370,21 +370,18 @@ __global__ void __maxnreg__(96) pop_bucket_kernel(const PopParams P) {
       st_hint_v4(reinterpret_cast<int4*>(orow + 4 * (int64_t)c), make_int4(ov[0], ov[1], ov[2], ov[3]), pol_stream);
     }
   } else {
-    // index ring: slot j holds the indexes of the chunk c with c % 2 == j, loaded two chunks
-    // (eight steps) ahead
-    int4 kr[2];
-#pragma unroll
-    for (int j = 0; j < 2; ++j) kr[j] = j < nch ? ld_idx4(irow + 4 * j, pol_stream) : make_int4(0, 0, 0, 0);
-    uintptr_t a = (bk0 + (uintptr_t)min((uint32_t)kr[0].x, kmark) * rowbytes) | ((((uint32_t)x) >> 1) & bmask);
+    // indexes two chunks (eight steps) ahead: kn0 holds chunk c + 1, kn1 chunk c + 2 (the copy
+    // kn0 = kn1 reads a load issued a whole chunk earlier)
+    int4 kn0 = nch > 0 ? ld_idx4(irow, pol_stream) : make_int4(0, 0, 0, 0);
+    int4 kn1 = nch > 1 ? ld_idx4(irow + 4, pol_stream) : make_int4(0, 0, 0, 0);
+    uintptr_t a = (bk0 + (uintptr_t)min((uint32_t)kn0.x, kmark) * rowbytes) | ((((uint32_t)x) >> 1) & bmask);
 #pragma unroll 1
-    for (int c0 = 0; c0 < nch; c0 += 2) {
-#pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        const int c = c0 + j;
-        if (c >= nch) break;
-        const int4 k4 = kr[j];
-        const int32_t knext = kr[j ^ 1].x;  // first index of chunk c + 1
-        if (c + 2 < nch) kr[j] = ld_idx4(irow + 4 * (int64_t)(c + 2), pol_stream);
+    for (int c = 0; c < nch; ++c) {
+      {
+        const int4 k4 = kn0;
+        kn0 = kn1;
+        const int32_t knext = kn0.x;  // first index of chunk c + 1
+        if (c + 2 < nch) kn1 = ld_idx4(irow + 4 * (int64_t)(c + 2), pol_stream);
         const int32_t kv[5] = {k4.x, k4.y, k4.z, k4.w, knext};
         // table offsets (and escape slots) of the chunk's four steps, read only when some table
         // has an offset or escapes are coded (a block-uniform branch, once per chunk)
