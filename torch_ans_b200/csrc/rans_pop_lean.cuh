@@ -258,6 +258,14 @@ __device__ __noinline__ LeanState<V> popb_rare(const PopParams P, LeanState<V> s
   return popl_exact<V, LK, BYPASS, TM_BUCKET_GLOBAL>(P, st, row, k, tsm, nullptr, nullptr);
 }
 
+// Bucket entry at address `a`; volatile, so the compiler keeps it where it is written (ahead of
+// the rare-step branch) instead of moving it into the branch's fall-through path
+__device__ __forceinline__ unsigned long long ld_entry(uintptr_t a, unsigned long long policy) {
+  unsigned long long v;
+  asm volatile("ld.global.nc.L2::cache_hint.u64 %0, [%1], %2;\n" : "=l"(v) : "l"(a), "l"(policy));
+  return v;
+}
+
 // Stream word at p when `pred`, else `w` (a predicated load, zero-extended: no branch on the
 // serial step)
 __device__ __forceinline__ uint32_t ld_word_if(const uint32_t* p, bool pred, uint32_t w) {
@@ -289,14 +297,15 @@ __device__ __forceinline__ uint32_t ld_word_if(const uint8_t* p, bool pred, uint
 // remaining cases by the exact step).  The serial chain of a step is
 //   entry load -> up = (cum << 16) > lo, one compare on the loaded word -> freq = up ? f1 : f0,
 //   offset = cum - c1 + (up ? 0 : f0) -> x = freq * (x >> fp) + offset -> refill test ->
-//   next entry address,
+//   next entry address -> next entry load (issued before the step's rare-step branch, so the
+//   branch resolves in the load's shadow; the rare step reissues it),
 // where the next address is a select between the two candidates computed beside the refill test
 // (refill: the low word becomes the prefetched stream word; else the low word of the product),
 // each a row address OR-ed with (low word >> 1) & mask: rows are aligned to their size, so the OR
 // is the add.  A row of markers after the last table stands for table indexes outside the table
 // list, so the marker test is the step's only check.  Off the chain: symbol output and table
-// offsets (read only when some table has a non-zero offset, or for the escape slot), index loads
-// two chunks ahead in a fixed ring of registers, the predicated prefetch of the next stream word,
+// offsets (read once per chunk, only when some table has a non-zero offset or escapes are coded),
+// index loads two chunks ahead, the predicated prefetch of the next stream word,
 // and the underflow test, made once at the end of the stream (a refill read below the first data
 // word happened exactly when the cursor fell below first - 1).
 template <int V, int LK, bool BYPASS>
@@ -375,6 +384,9 @@ __global__ void __maxnreg__(96) pop_bucket_kernel(const PopParams P) {
     int4 kn0 = nch > 0 ? ld_idx4(irow, pol_stream) : make_int4(0, 0, 0, 0);
     int4 kn1 = nch > 1 ? ld_idx4(irow + 4, pol_stream) : make_int4(0, 0, 0, 0);
     uintptr_t a = (bk0 + (uintptr_t)min((uint32_t)kn0.x, kmark) * rowbytes) | ((((uint32_t)x) >> 1) & bmask);
+    // the entry of the next step: each step issues the next step's load before its own rare-step
+    // branch, so the branch resolves while the load is in flight (the rare step reissues it)
+    unsigned long long en = ld_entry(a, pol_keep);
 #pragma unroll 1
     for (int c = 0; c < nch; ++c) {
       {
@@ -402,7 +414,7 @@ __global__ void __maxnreg__(96) pop_bucket_kernel(const PopParams P) {
           const S x0 = x;
           const uint32_t w0 = nextw;
           const int p0 = p;
-          const unsigned long long e = ld_hint_u64(reinterpret_cast<const unsigned long long*>(a), pol_keep);
+          const unsigned long long e = en;
           const uint32_t cum = (uint32_t)x & cmask;
           const S xs = x >> P.fp;
           const uint32_t lo = (uint32_t)e, hi = (uint32_t)(e >> 32);
@@ -436,8 +448,7 @@ __global__ void __maxnreg__(96) pop_bucket_kernel(const PopParams P) {
             a = rown | ((((uint32_t)x) >> 1) & bmask);
           }
           ov[q] = (int32_t)(sv + (uint32_t)ofs[q]);
-          // the fast step above is computed before the branch, so the branch is off its chain
-          asm volatile("" ::"l"((unsigned long long)a), "l"((unsigned long long)x));
+          en = ld_entry(a, pol_keep);  // every address is a row plus a masked offset: inside the table
           if (slow) {
             LeanState<V> st{x0, (S)w0, (long long)p0, err, 0};
             st = popb_rare<V, LK, BYPASS>(P, st, row, k, e, tsm);
@@ -447,6 +458,7 @@ __global__ void __maxnreg__(96) pop_bucket_kernel(const PopParams P) {
             err = st.err;
             ov[q] = st.v;
             a = rown | ((((uint32_t)x) >> 1) & bmask);
+            en = ld_entry(a, pol_keep);
           }
         }
         st_hint_v4(reinterpret_cast<int4*>(orow + 4 * (int64_t)c), make_int4(ov[0], ov[1], ov[2], ov[3]), pol_stream);
