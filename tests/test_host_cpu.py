@@ -183,3 +183,42 @@ def test_parse_merged_matches_split_merged_bytes(prefix):
     if prefix > 1:  # a data tail shorter than one prefix
         with pytest.raises(RuntimeError, match="truncated"):
             _C.parse_merged(torch.frombuffer(bytearray(b"\x01" * (prefix - 1)), dtype=torch.uint8), prefix, 1)
+
+
+def _reference_bisection(row, size, cum, fp):
+    """The search of rans_pop_step (rans_utils.hpp:424-450): first probe (size * cum) >> fp, then
+    bisection on [0, size - 1]; returns s = idx - 1."""
+    idx = (size * cum) >> fp
+    low, high = 0, size - 1
+    while high > low:
+        if cum >= row[idx]:
+            low = idx + 1
+        else:
+            high = idx
+        idx = (low + high) // 2
+    return idx - 1
+
+
+def test_ballot_prefix_rule_equals_reference_bisection():
+    """The ragged warp pop decodes s = popc(m) - 1 from the ballot m of row[j] <= cum (j < size)
+    when bit 0 is set, bit size - 1 is clear and the set bits form a prefix; on every such mask the
+    reference's bisection must end at the same s, for monotone and non-monotone rows alike."""
+    import numpy as np
+    rng = np.random.default_rng(7)
+    fp = 8
+    fired = 0
+    for trial in range(300):
+        size = int(rng.integers(2, 34))
+        if trial % 3 == 0:
+            row = np.sort(rng.integers(0, 1 << fp, size))
+        else:  # non-monotone rows, values spread over the cum range
+            row = rng.integers(0, 1 << fp, size)
+        for cum in range(1 << fp):
+            m = 0
+            for j in range(size):
+                if row[j] <= cum:
+                    m |= 1 << j
+            if (m & 1) and not (m >> (size - 1)) & 1 and (m & (m + 1)) == 0:
+                fired += 1
+                assert bin(m).count("1") - 1 == _reference_bisection(row, size, cum, fp), (row, size, cum)
+    assert fired > 1000

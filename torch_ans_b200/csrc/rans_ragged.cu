@@ -276,13 +276,16 @@ __global__ void __launch_bounds__(256) ragged_pop_kernel(const RaggedArgs R, con
 }
 
 // One warp per stream, for rows of at most 64 entries (the per-element tables: 33 entries).  Lane
-// l stages entries l and l + 32 of each step's row with 4-byte cp.async RW_D steps ahead (each lane
-// reads back only what it copied itself, so no cross-lane ordering is needed); the search is a
-// ballot (size and offset are staged by lane 0 and broadcast): for a row that is non-decreasing with row[0] <= cum < row[size - 1], the reference's
-// bisection (rans_utils.hpp:424-450) ends at the count of entries j < size - 1 with row[j] <= cum,
-// so s = count - 1 and (start, freq) come from two shuffles.  A row failing that test takes the
-// reference bisection itself (on the staged row).  Every lane carries the same state; the decoded
-// symbols of 32 steps leave as one coalesced store.
+// l stages entries l and l + 32 of each step's row with 4-byte cp.async RW_D steps ahead (lane 0
+// also the row's size and offset); after its own copies land each lane meets the others at a
+// __syncwarp, so entries staged by another lane are visible.  The search is one ballot of
+// P(j) = row[j] <= cum over the row's entries j < size: the reference's bisection
+// (rans_utils.hpp:424-450) keeps low <= c <= high for every probe whenever P is true exactly on
+// the first c entries and false on entry size - 1, so it ends at s = c - 1 whatever the row's
+// values are; the ballot mask shows that case directly (bit 0 set, bit size - 1 clear, set bits a
+// prefix: m & (m + 1) == 0), s = popc(m) - 1 and (start, freq) come from two shuffles.  Any other
+// mask takes the reference bisection itself (on the staged row).  Every lane carries the same
+// state; the decoded symbols of 32 steps leave as one coalesced store.
 constexpr int RW_D = 12;   // steps between a row copy and its use
 constexpr int RW_R = 16;   // row ring slots per warp (> RW_D)
 constexpr int RW_E = 66;   // staged words per slot: 64 entries + size + offset
@@ -368,33 +371,25 @@ __global__ void __launch_bounds__(256) ragged_pop_warp_kernel(const RaggedArgs R
       if constexpr (!WIDE) {
         // rows of at most 33 entries: lane l holds entry l, every lane reads entry 32
         const int32_t e32 = W > 32 ? slot[32] : 0;
-        const int32_t n0 = __shfl_down_sync(0xffffffffu, c0, 1);
-        const int32_t next0 = lane == 31 ? e32 : n0;
-        const bool mono = lane + 1 >= size || c0 <= next0;
-        const int32_t lastv = size - 1 == 32 ? e32 : __shfl_sync(0xffffffffu, c0, (size - 1) & 31);
-        const int32_t firstv = __shfl_sync(0xffffffffu, c0, 0);
-        fast = size >= 2 && size <= W && __all_sync(0xffffffffu, mono) && firstv <= cum && cum < lastv;
+        const unsigned m = __ballot_sync(0xffffffffu, lane < size && c0 <= cum);
+        // P(size - 1) must be false: bit size - 1 of the mask, or entry 32 for 33-entry rows
+        const bool last_false = size <= 32 ? ((m >> ((size - 1) & 31)) & 1u) == 0u : cum < e32;
+        fast = size >= 2 && size <= W && (m & 1u) != 0u && (m & (m + 1u)) == 0u && last_false;
         if (fast) {
-          s = __popc(__ballot_sync(0xffffffffu, lane < size - 1 && c0 <= cum)) - 1;
+          s = __popc(m) - 1;
           st = __shfl_sync(0xffffffffu, c0, (int)s);
           const int32_t en0 = __shfl_sync(0xffffffffu, c0, (int)(s + 1) & 31);
           en = s + 1 == 32 ? e32 : en0;
         }
       } else {
         const int32_t c1 = lane + 32 < W ? slot[32 + lane] : 0;
-        const int32_t n0 = __shfl_down_sync(0xffffffffu, c0, 1);
-        const int32_t c1_first = __shfl_sync(0xffffffffu, c1, 0);
-        const int32_t n1 = __shfl_down_sync(0xffffffffu, c1, 1);
-        const int32_t next0 = lane == 31 ? c1_first : n0;
-        const bool mono = (lane + 1 >= size || c0 <= next0) && (lane + 33 >= size || c1 <= n1);
-        const int32_t lastv =
-            size >= 1 && size <= 64 ? __shfl_sync(0xffffffffu, size - 1 < 32 ? c0 : c1, (size - 1) & 31) : 0;
-        const int32_t firstv = __shfl_sync(0xffffffffu, c0, 0);
-        fast = size >= 2 && size <= W && __all_sync(0xffffffffu, mono) && firstv <= cum && cum < lastv;
+        const unsigned m0 = __ballot_sync(0xffffffffu, lane < size && c0 <= cum);
+        const unsigned m1 = __ballot_sync(0xffffffffu, lane + 32 < size && c1 <= cum);
+        const unsigned long long mm = (unsigned long long)m0 | ((unsigned long long)m1 << 32);
+        fast = size >= 2 && size <= W && (mm & 1ull) != 0ull && (mm & (mm + 1ull)) == 0ull &&
+               ((mm >> ((size - 1) & 63)) & 1ull) == 0ull;
         if (fast) {
-          const unsigned m0 = __ballot_sync(0xffffffffu, lane < size - 1 && c0 <= cum);
-          const unsigned m1 = __ballot_sync(0xffffffffu, lane + 32 < size - 1 && c1 <= cum);
-          s = __popc(m0) + __popc(m1) - 1;
+          s = __popcll(mm) - 1;
           st = __shfl_sync(0xffffffffu, s < 32 ? c0 : c1, (int)(s & 31));
           en = __shfl_sync(0xffffffffu, s + 1 < 32 ? c0 : c1, (int)((s + 1) & 31));
         }
