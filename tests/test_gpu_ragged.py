@@ -151,12 +151,13 @@ def test_ragged_bad_rows_and_indexes_are_flagged(variant):
 
 
 @pytest.mark.parametrize("variant", VARIANTS)
-@pytest.mark.parametrize("case", ["unsorted_rows", "wide_rows"])
+@pytest.mark.parametrize("case", ["unsorted_rows", "wide_rows", "short_table"])
 def test_ragged_pop_unusual_rows(variant, case):
     """Rows the ballot search must not take (entries out of order: the reference bisection's
-    answer then differs from a count, so the kernel runs the bisection itself), and rows wider than
-    64 entries (the thread-per-stream kernel).  Decoded symbols, rows and error bits must match
-    the oracle's per-stream pops of the same streams."""
+    answer then differs from a count unless the comparison mask is still a prefix, so the kernel
+    runs the bisection itself), rows wider than 64 entries (the thread-per-stream kernel), and a
+    per-element table list shorter than the symbols (the steps past it are bad indexes).  Decoded
+    symbols, rows and error bits must match the oracle's per-stream pops of the same streams."""
     from torch_ans_b200 import _C
     rng = np.random.default_rng(zlib.crc32(f"unusual-{variant}-{case}".encode()))
     lengths = [0, 1, 9, 40, 33, 70, 3]
@@ -168,14 +169,16 @@ def test_ragged_pop_unusual_rows(variant, case):
         for i in range(0, len(sym), 3):
             a, b = 5 + i % 7, 20 + i % 9
             pop_cdfs[i, a], pop_cdfs[i, b] = pop_cdfs[i, b], pop_cdfs[i, a]
-    # oracle pops of each stream with the (possibly unsorted) rows
+    if case == "short_table":  # the last 50 symbols have no row
+        pop_cdfs, sizes, offs = pop_cdfs[:-50].copy(), sizes[:-50].copy(), offs[:-50].copy()
+    # oracle pops of each stream with the (possibly unsorted) rows; symbol i of the batch reads row i
     dec_ref, rows_ref, err_ref = [], [], 0
     lo = 0
     for b, n in enumerate(lengths):
         st = pushed[b].copy()
         if n:
-            d, e = O.pop(variant, st, np.arange(n, dtype=np.int32)[None], pop_cdfs[lo:lo + n], sizes[lo:lo + n],
-                         offs[lo:lo + n], fp, False)
+            d, e = O.pop(variant, st, np.arange(lo, lo + n, dtype=np.int32)[None], pop_cdfs, sizes, offs, fp,
+                         False)
             dec_ref.append(d.reshape(-1))
             err_ref |= e
         rows_ref.append(st)

@@ -290,13 +290,19 @@ constexpr int RW_D = 12;   // steps between a row copy and its use
 constexpr int RW_R = 16;   // row ring slots per warp (> RW_D)
 constexpr int RW_E = 66;   // staged words per slot: 64 entries + size + offset
 
-template <int V, bool BYPASS, bool WIDE>
+// shared-memory words per warp: a ring of RW_R row slots, or (consecutive rows) two buffers of
+// 32 rows with their sizes and offsets
+__host__ __device__ inline size_t ragged_warp_words(bool contig, int64_t cdf_width) {
+  return contig ? 2 * (32 * (size_t)cdf_width + 64) : (size_t)RW_R * RW_E;
+}
+
+template <int V, bool BYPASS, bool WIDE, bool CONTIG>
 __global__ void __launch_bounds__(256) ragged_pop_warp_kernel(const RaggedArgs R, const PopParams P) {
   using S = typename VT<V>::State;
   using Wd = typename VT<V>::Word;
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const int warps = blockDim.x >> 5, wib = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  int32_t* ring = reinterpret_cast<int32_t*>(smem_raw) + (size_t)wib * RW_R * RW_E;
+  int32_t* ring = reinterpret_cast<int32_t*>(smem_raw) + (size_t)wib * ragged_warp_words(CONTIG, R.cdf_width);
   const int64_t b = (int64_t)blockIdx.x * warps + wib;
   if (b >= R.batch) return;
   int64_t lo, hi;
@@ -317,134 +323,184 @@ __global__ void __launch_bounds__(256) ragged_pop_warp_kernel(const RaggedArgs R
   const int n = (int)(hi - lo);
   const int W = (int)R.cdf_width;
   const int32_t cmask = (int32_t)((1u << R.fp) - 1u);
+  // one step decoded from a staged row (`slot`: the row's entries in shared memory)
+  auto decode = [&](const int32_t* slot, int32_t size, int32_t offset) -> int32_t {
+    int32_t v = 0;
+    const int32_t cum = (int32_t)((uint32_t)x & (uint32_t)cmask);
+    const int32_t c0 = lane < W ? slot[lane] : 0;
+    int64_t s;
+    int32_t cum_off = 0, freq = 0;
+    bool found;
+    bool fast;
+    int32_t st = 0, en = 0;
+    if constexpr (!WIDE) {
+      // rows of at most 33 entries: lane l holds entry l, every lane reads entry 32
+      const int32_t e32 = W > 32 ? slot[32] : 0;
+      const unsigned m = __ballot_sync(0xffffffffu, lane < size && c0 <= cum);
+      // P(size - 1) must be false: bit size - 1 of the mask, or entry 32 for 33-entry rows
+      const bool last_false = size <= 32 ? ((m >> ((size - 1) & 31)) & 1u) == 0u : cum < e32;
+      fast = size >= 2 && size <= W && (m & 1u) != 0u && (m & (m + 1u)) == 0u && last_false;
+      if (fast) {
+        s = __popc(m) - 1;
+        st = __shfl_sync(0xffffffffu, c0, (int)s);
+        const int32_t en0 = __shfl_sync(0xffffffffu, c0, (int)(s + 1) & 31);
+        en = s + 1 == 32 ? e32 : en0;
+      }
+    } else {
+      const int32_t c1 = lane + 32 < W ? slot[32 + lane] : 0;
+      const unsigned m0 = __ballot_sync(0xffffffffu, lane < size && c0 <= cum);
+      const unsigned m1 = __ballot_sync(0xffffffffu, lane + 32 < size && c1 <= cum);
+      const unsigned long long mm = (unsigned long long)m0 | ((unsigned long long)m1 << 32);
+      fast = size >= 2 && size <= W && (mm & 1ull) != 0ull && (mm & (mm + 1ull)) == 0ull &&
+             ((mm >> ((size - 1) & 63)) & 1ull) == 0ull;
+      if (fast) {
+        s = __popcll(mm) - 1;
+        st = __shfl_sync(0xffffffffu, s < 32 ? c0 : c1, (int)(s & 31));
+        en = __shfl_sync(0xffffffffu, s + 1 < 32 ? c0 : c1, (int)((s + 1) & 31));
+      }
+    }
+    if (fast) {
+      cum_off = cum - st;
+      freq = (int32_t)((uint32_t)en - (uint32_t)st);
+      found = true;
+    } else {
+      TableInfo tinf;
+      tinf.size = size;
+      tinf.offset = offset;
+      tinf.cut = 0;
+      tinf.cut_log2 = -1;
+      found = lookup_symbol<V, LK_SEARCH, false>(slot, tinf, cum, R.cdf_width, R.fp, s, cum_off, freq);
+    }
+    if (!found) {
+      err |= DEV_BAD_VALUE;
+    } else {
+      // x = D(x) and the refill (rans_utils.hpp:473-475), the first word from the prefetch
+      x = (S)((x >> R.fp) * to_state<S>(freq) + to_state<S>(cum_off));
+#pragma unroll
+      for (int t = 0; t < VT<V>::MAX_RENORM; ++t) {
+        if ((unsigned long long)x < VT<V>::LB) {
+          if (p < first || p >= capw) err |= DEV_UNDERFLOW;
+          x = (S)((x << VT<V>::WB) | nextw);
+          --p;
+          nextw = (p >= first && p < capw) ? (S)__ldg(pw + p) : (S)0;
+        }
+      }
+      int32_t value = (int32_t)s;
+      if constexpr (BYPASS) {
+        if (value == size - 2) {  // escape (rare): the cursor-based reference code
+          PopCursor<V> cur;
+          cur.payload = reinterpret_cast<const uint8_t*>(row + 1);
+          cur.p = p;
+          cur.first = first;
+          cur.cap = (R.width - 1) * 4 / VT<V>::WBYTES;
+          cur.err = err;
+          const int32_t raw = pop_escape<V>(x, cur, R.bp);
+          value = raw >> 1;
+          value = (raw & 1) ? (-value - 1) : (value + size - 2);
+          p = (int)min(max(cur.p, (int64_t)-0x7fffffff), (int64_t)0x7fffffff);
+          err = cur.err;
+          nextw = (p >= first && p < capw) ? (S)__ldg(pw + p) : (S)0;
+        }
+      }
+      v = (int32_t)((uint32_t)value + (uint32_t)offset);
+    }
+    return v;
+  };
   int32_t kcur = 0;   // table index held by this lane for steps [32 m, 32 m + 32)
   int32_t outv = 0;   // decoded symbol of step 32 m + lane
-  auto table_at = [&](int t, int32_t kreg) -> int64_t {
-    return R.idx ? (int64_t)__shfl_sync(0xffffffffu, kreg, t & 31) : lo + t;
-  };
-  int32_t kahead = (R.idx && lane < n) ? R.idx[lo + lane] : 0;           // indexes of steps [0, 32)
-  int32_t kahead2 = (R.idx && 32 + lane < n) ? R.idx[lo + 32 + lane] : 0;  // steps [32, 64)
-  // iteration j: stage the row of step j, decode step j - RW_D
-  for (int j = 0; j < n + RW_D; ++j) {
-    if ((j & 31) == 0 && j > 0) {  // rotate the index registers every 32 steps
-      kahead = kahead2;
-      kahead2 = (R.idx && j + 32 + lane < n) ? R.idx[lo + j + 32 + lane] : 0;
-    }
-    if (j < n) {
-      const int64_t k = table_at(j, kahead);
-      int32_t* slot = ring + (j & (RW_R - 1)) * RW_E;
-      if (k >= 0 && k < R.ntables) {
-        const int32_t* src = R.cdfs + k * R.cdf_width;
-        if (lane < W) cp_async4(slot + lane, src + lane);
-        if (lane + 32 < W) cp_async4(slot + 32 + lane, src + 32 + lane);
-        if (lane == 0) {
-          cp_async4(slot + 64, R.sizes + k);
-          if (R.offsets) cp_async4(slot + 65, R.offsets + k);
-        }
+  if constexpr (CONTIG) {
+    // rows of consecutive symbols are consecutive: stage 32 steps' rows (with their sizes and
+    // offsets) at once into one of two buffers, one block ahead of the decode
+    int32_t* bufs[2] = {ring, ring + (32 * W + 64)};
+    const int nblk = (n + 31) >> 5;
+    auto stage = [&](int blk) {
+      int32_t* buf = bufs[blk & 1];
+      const int64_t t0 = lo + ((int64_t)blk << 5);
+      const int nr = min(32, n - (blk << 5));
+      const int vr = (int)max((int64_t)0, min((int64_t)nr, R.ntables - t0));  // rows inside the table list
+      const int32_t* src = R.cdfs + t0 * R.cdf_width;
+      for (int i = lane; i < vr * W; i += 32) cp_async4(buf + i, src + i);
+      if (lane < vr) {
+        cp_async4(buf + 32 * W + lane, R.sizes + t0 + lane);
+        if (R.offsets) cp_async4(buf + 32 * W + 32 + lane, R.offsets + t0 + lane);
       }
-    }
+    };
+    if (nblk > 0) stage(0);
     cp_async_commit();
-    const int tc = j - RW_D;
-    if (tc < 0) continue;
-    if ((tc & 31) == 0) {
-      if (tc > 0) R.out[lo + tc - 32 + lane] = outv;  // the previous 32 steps: one coalesced store
-      // indexes of steps [tc, tc + 32): the staging side (RW_D < 32 steps ahead) holds them now
-      kcur = kahead;
+    for (int blk = 0; blk < nblk; ++blk) {
+      if (blk + 1 < nblk) stage(blk + 1);
+      cp_async_commit();
+      cp_async_wait<1>();
+      __syncwarp();  // every lane's staged words are visible to the whole warp
+      const int32_t* buf = bufs[blk & 1];
+      const int t0 = blk << 5;
+      const int nr = min(32, n - t0);
+#pragma unroll 1
+      for (int r = 0; r < nr; ++r) {
+        int32_t v = 0;
+        if (lo + t0 + r >= R.ntables) {
+          err |= DEV_BAD_INDEX;
+        } else {
+          const int32_t size = buf[32 * W + r];
+          const int32_t offset = R.offsets ? buf[32 * W + 32 + r] : 0;
+          v = decode(buf + r * W, size, offset);
+        }
+        if (r == lane) outv = v;
+      }
+      if (lane < nr) R.out[lo + t0 + lane] = outv;  // one coalesced store per block
+      __syncwarp();  // the buffer is restaged only after every lane has read it
     }
-    cp_async_wait<RW_D - 1>();
-    __syncwarp();  // every lane's staged words are visible to the whole warp
-    const int64_t k = table_at(tc, kcur);
-    int32_t v = 0;
-    if (k < 0 || k >= R.ntables) {
-      err |= DEV_BAD_INDEX;
-    } else {
-      const int32_t* slot = ring + (tc & (RW_R - 1)) * RW_E;
-      const int32_t size = __shfl_sync(0xffffffffu, lane == 0 ? slot[64] : 0, 0);
-      const int32_t offset = R.offsets ? __shfl_sync(0xffffffffu, lane == 0 ? slot[65] : 0, 0) : 0;
-      const int32_t cum = (int32_t)((uint32_t)x & (uint32_t)cmask);
-      const int32_t c0 = lane < W ? slot[lane] : 0;
-      int64_t s;
-      int32_t cum_off = 0, freq = 0;
-      bool found;
-      bool fast;
-      int32_t st = 0, en = 0;
-      if constexpr (!WIDE) {
-        // rows of at most 33 entries: lane l holds entry l, every lane reads entry 32
-        const int32_t e32 = W > 32 ? slot[32] : 0;
-        const unsigned m = __ballot_sync(0xffffffffu, lane < size && c0 <= cum);
-        // P(size - 1) must be false: bit size - 1 of the mask, or entry 32 for 33-entry rows
-        const bool last_false = size <= 32 ? ((m >> ((size - 1) & 31)) & 1u) == 0u : cum < e32;
-        fast = size >= 2 && size <= W && (m & 1u) != 0u && (m & (m + 1u)) == 0u && last_false;
-        if (fast) {
-          s = __popc(m) - 1;
-          st = __shfl_sync(0xffffffffu, c0, (int)s);
-          const int32_t en0 = __shfl_sync(0xffffffffu, c0, (int)(s + 1) & 31);
-          en = s + 1 == 32 ? e32 : en0;
-        }
-      } else {
-        const int32_t c1 = lane + 32 < W ? slot[32 + lane] : 0;
-        const unsigned m0 = __ballot_sync(0xffffffffu, lane < size && c0 <= cum);
-        const unsigned m1 = __ballot_sync(0xffffffffu, lane + 32 < size && c1 <= cum);
-        const unsigned long long mm = (unsigned long long)m0 | ((unsigned long long)m1 << 32);
-        fast = size >= 2 && size <= W && (mm & 1ull) != 0ull && (mm & (mm + 1ull)) == 0ull &&
-               ((mm >> ((size - 1) & 63)) & 1ull) == 0ull;
-        if (fast) {
-          s = __popcll(mm) - 1;
-          st = __shfl_sync(0xffffffffu, s < 32 ? c0 : c1, (int)(s & 31));
-          en = __shfl_sync(0xffffffffu, s + 1 < 32 ? c0 : c1, (int)((s + 1) & 31));
-        }
+  } else {
+    auto table_at = [&](int t, int32_t kreg) -> int64_t {
+      return R.idx ? (int64_t)__shfl_sync(0xffffffffu, kreg, t & 31) : lo + t;
+    };
+    int32_t kahead = (R.idx && lane < n) ? R.idx[lo + lane] : 0;           // indexes of steps [0, 32)
+    int32_t kahead2 = (R.idx && 32 + lane < n) ? R.idx[lo + 32 + lane] : 0;  // steps [32, 64)
+    // iteration j: stage the row of step j, decode step j - RW_D
+    for (int j = 0; j < n + RW_D; ++j) {
+      if ((j & 31) == 0 && j > 0) {  // rotate the index registers every 32 steps
+        kahead = kahead2;
+        kahead2 = (R.idx && j + 32 + lane < n) ? R.idx[lo + j + 32 + lane] : 0;
       }
-      if (fast) {
-        cum_off = cum - st;
-        freq = (int32_t)((uint32_t)en - (uint32_t)st);
-        found = true;
-      } else {
-        TableInfo tinf;
-        tinf.size = size;
-        tinf.offset = offset;
-        tinf.cut = 0;
-        tinf.cut_log2 = -1;
-        found = lookup_symbol<V, LK_SEARCH, false>(slot, tinf, cum, R.cdf_width, R.fp, s, cum_off, freq);
-      }
-      if (!found) {
-        err |= DEV_BAD_VALUE;
-      } else {
-        // x = D(x) and the refill (rans_utils.hpp:473-475), the first word from the prefetch
-        x = (S)((x >> R.fp) * to_state<S>(freq) + to_state<S>(cum_off));
-#pragma unroll
-        for (int t = 0; t < VT<V>::MAX_RENORM; ++t) {
-          if ((unsigned long long)x < VT<V>::LB) {
-            if (p < first || p >= capw) err |= DEV_UNDERFLOW;
-            x = (S)((x << VT<V>::WB) | nextw);
-            --p;
-            nextw = (p >= first && p < capw) ? (S)__ldg(pw + p) : (S)0;
+      if (j < n) {
+        const int64_t k = table_at(j, kahead);
+        int32_t* slot = ring + (j & (RW_R - 1)) * RW_E;
+        if (k >= 0 && k < R.ntables) {
+          const int32_t* src = R.cdfs + k * R.cdf_width;
+          if (lane < W) cp_async4(slot + lane, src + lane);
+          if (lane + 32 < W) cp_async4(slot + 32 + lane, src + 32 + lane);
+          if (lane == 0) {
+            cp_async4(slot + 64, R.sizes + k);
+            if (R.offsets) cp_async4(slot + 65, R.offsets + k);
           }
         }
-        int32_t value = (int32_t)s;
-        if constexpr (BYPASS) {
-          if (value == size - 2) {  // escape (rare): the cursor-based reference code
-            PopCursor<V> cur;
-            cur.payload = reinterpret_cast<const uint8_t*>(row + 1);
-            cur.p = p;
-            cur.first = first;
-            cur.cap = (R.width - 1) * 4 / VT<V>::WBYTES;
-            cur.err = err;
-            const int32_t raw = pop_escape<V>(x, cur, R.bp);
-            value = raw >> 1;
-            value = (raw & 1) ? (-value - 1) : (value + size - 2);
-            p = (int)min(max(cur.p, (int64_t)-0x7fffffff), (int64_t)0x7fffffff);
-            err = cur.err;
-            nextw = (p >= first && p < capw) ? (S)__ldg(pw + p) : (S)0;
-          }
-        }
-        v = (int32_t)((uint32_t)value + (uint32_t)offset);
       }
+      cp_async_commit();
+      const int tc = j - RW_D;
+      if (tc < 0) continue;
+      if ((tc & 31) == 0) {
+        if (tc > 0) R.out[lo + tc - 32 + lane] = outv;  // the previous 32 steps: one coalesced store
+        // indexes of steps [tc, tc + 32): the staging side (RW_D < 32 steps ahead) holds them now
+        kcur = kahead;
+      }
+      cp_async_wait<RW_D - 1>();
+      __syncwarp();  // every lane's staged words are visible to the whole warp
+      const int64_t k = table_at(tc, kcur);
+      int32_t v = 0;
+      if (k < 0 || k >= R.ntables) {
+        err |= DEV_BAD_INDEX;
+      } else {
+        const int32_t* slot = ring + (tc & (RW_R - 1)) * RW_E;
+        const int32_t size = __shfl_sync(0xffffffffu, lane == 0 ? slot[64] : 0, 0);
+        const int32_t offset = R.offsets ? __shfl_sync(0xffffffffu, lane == 0 ? slot[65] : 0, 0) : 0;
+        v = decode(slot, size, offset);
+      }
+      if ((tc & 31) == lane) outv = v;
     }
-    if ((tc & 31) == lane) outv = v;
+    // the last group of decoded symbols (full or partial)
+    const int last = n > 0 ? ((n - 1) & ~31) : 0;
+    if (n > 0 && last + lane < n) R.out[lo + last + lane] = outv;
   }
-  // the last group of decoded symbols (full or partial)
-  const int last = n > 0 ? ((n - 1) & ~31) : 0;
-  if (n > 0 && last + lane < n) R.out[lo + last + lane] = outv;
   cp_async_wait<0>();
   if (lane == 0) {
     store_state<V>(row, 0, x);
@@ -477,21 +533,30 @@ static void ragged_push_launch(const RaggedArgs& R, const PushParams& P, int sms
   note_launch();
 }
 
-template <int V, bool BY, bool WIDE>
+template <int V, bool BY, bool WIDE, bool CONTIG>
 static void ragged_pop_warp_go(const RaggedArgs& R, const PopParams& P, int sms, cudaStream_t s) {
   int64_t warps = (R.batch + sms - 1) / sms;
   warps = std::max<int64_t>(1, std::min<int64_t>(warps, 8));
-  const size_t smem = (size_t)warps * RW_R * RW_E * sizeof(int32_t);
+  const size_t smem = (size_t)warps * ragged_warp_words(CONTIG, R.cdf_width) * sizeof(int32_t);
   if (smem > 48 * 1024)
-    cudaFuncSetAttribute(ragged_pop_warp_kernel<V, BY, WIDE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  ragged_pop_warp_kernel<V, BY, WIDE><<<(int)((R.batch + warps - 1) / warps), (int)(warps * 32), smem, s>>>(R, P);
+    cudaFuncSetAttribute(ragged_pop_warp_kernel<V, BY, WIDE, CONTIG>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)smem);
+  ragged_pop_warp_kernel<V, BY, WIDE, CONTIG>
+      <<<(int)((R.batch + warps - 1) / warps), (int)(warps * 32), smem, s>>>(R, P);
   note_launch();
 }
 
+// without table indexes the rows of consecutive symbols are consecutive: block staging
 template <int V, bool BY>
 static void ragged_pop_warp_launch(const RaggedArgs& R, const PopParams& P, int sms, cudaStream_t s) {
-  if (R.cdf_width <= 33) ragged_pop_warp_go<V, BY, false>(R, P, sms, s);
-  else ragged_pop_warp_go<V, BY, true>(R, P, sms, s);
+  const bool contig = R.idx == nullptr;
+  if (R.cdf_width <= 33) {
+    if (contig) ragged_pop_warp_go<V, BY, false, true>(R, P, sms, s);
+    else ragged_pop_warp_go<V, BY, false, false>(R, P, sms, s);
+  } else {
+    if (contig) ragged_pop_warp_go<V, BY, true, true>(R, P, sms, s);
+    else ragged_pop_warp_go<V, BY, true, false>(R, P, sms, s);
+  }
 }
 
 template <int V, bool BY, bool STAGE>
