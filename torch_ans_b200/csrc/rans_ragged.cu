@@ -132,8 +132,14 @@ __global__ void __launch_bounds__(256) ragged_push_chain_kernel(const RaggedArgs
   cur.p = (int64_t)row[0] / VT<V>::WBYTES - 1;
   cur.cap = (R.width - 1) * 4 / VT<V>::WBYTES;
   cur.err = 0;
-  typename VT<V>::State x = load_state<V>(row, 0);
+  using S = typename VT<V>::State;
+  using W = typename VT<V>::Word;
+  constexpr int MR = VT<V>::MAX_RENORM;
+  S x = load_state<V>(row, 0);
   const int64_t n = hi - lo;
+  const bool packed = P.fp <= 23;
+  const int shift = VT<V>::USED - P.fp;
+  W* words = reinterpret_cast<W*>(cur.payload);
   for (int64_t t = 0; t < n + RG_D; ++t) {
     if (t < n) {  // step t codes symbol hi - 1 - t
       const int64_t i = hi - 1 - t;
@@ -153,7 +159,24 @@ __global__ void __launch_bounds__(256) ragged_push_chain_kernel(const RaggedArgs
     r.flags = (uint32_t)a.y;
     r.rbase = 0;
     r.rcap = 0;
-    push_chain<V, false, BYPASS>(P, x, cur, r);
+    const uint32_t freq = packed ? entry_freq(r.e, true) : 0u;
+    if (r.flags == 0u && freq != 0u && cur.p >= -1 && cur.p + MR < cur.cap) {
+      // every word this step can emit lands inside the row: the word goes to the next slot
+      // unconditionally and the cursor advances only when it is kept (a slot past the row's final
+      // length is never part of its record), so the renormalisation has no branch
+      const S bound = (S)((S)freq << shift);
+#pragma unroll
+      for (int u = 0; u < MR; ++u) {
+        const bool rn = x >= bound;
+        words[cur.p + 1] = (W)x;
+        cur.p += rn ? 1 : 0;
+        x = rn ? (S)(x >> VT<V>::WB) : x;
+      }
+      const S q = quotient<V>(x, r.e, true);
+      x = (S)(x + to_state<S>((int32_t)r.e.w) + q * (S)((S)((S)1 << P.fp) - (S)freq));
+    } else {
+      push_chain<V, false, BYPASS>(P, x, cur, r);  // flagged steps, rows near their end, wide precision
+    }
   }
   cp_async_wait<0>();
   store_state<V>(row, 0, x);
