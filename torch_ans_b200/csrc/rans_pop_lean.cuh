@@ -21,7 +21,9 @@
 namespace tans {
 
 // state of one stream that the rare exact step reads and writes (passed by value both ways, so the
-// kernel never takes the address of its state or of its parameters and keeps both in registers)
+// kernel never takes the address of its state and keeps it in registers); the kernel parameters
+// are __grid_constant__, so the out-of-line steps read them through a reference into the
+// parameter space instead of a copy on the stack
 template <int V> struct LeanState {
   typename VT<V>::State x, nextw;
   long long p;
@@ -31,7 +33,7 @@ template <int V> struct LeanState {
 
 // the reference-exact step of one symbol, out of line (rare path); refreshes the prefetched word
 template <int V, int LK, bool BYPASS, int TM>
-__device__ __noinline__ LeanState<V> popl_exact(const PopParams P, LeanState<V> st, const int32_t* row, int32_t k,
+__device__ __noinline__ LeanState<V> popl_exact(const PopParams& P, LeanState<V> st, const int32_t* row, int32_t k,
                                                 const TableInfo* tsm, const uint32_t* tD, const uint16_t* tS) {
   FastCursor<V> cur;
   cur.c.payload = reinterpret_cast<const uint8_t*>(row + 1);
@@ -59,7 +61,7 @@ __device__ __forceinline__ int4 ld_idx4(const int32_t* p, unsigned long long pol
 }
 
 template <int V, int LK, bool BYPASS, int TM>
-__global__ void __launch_bounds__(512) pop_lean_kernel(const PopParams P) {
+__global__ void __launch_bounds__(512) pop_lean_kernel(const __grid_constant__ PopParams P) {
   using S = typename VT<V>::State;
   using W = typename VT<V>::Word;
   extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -215,7 +217,7 @@ __global__ void __launch_bounds__(512) pop_lean_kernel(const PopParams P) {
 // secondary table's per-cum block) decode here with the same update and refill as the straight
 // step; everything else (type-0 markers, bad indexes, escapes) takes the exact step.
 template <int V, int LK, bool BYPASS>
-__device__ __noinline__ LeanState<V> popb_rare(const PopParams P, LeanState<V> st, const int32_t* row, int32_t k,
+__device__ __noinline__ LeanState<V> popb_rare(const PopParams& P, LeanState<V> st, const int32_t* row, int32_t k,
                                                unsigned long long e, const TableInfo* tsm) {
   using S = typename VT<V>::State;
   const uint32_t kind = (uint32_t)(e >> 16) & 3u;
@@ -309,7 +311,7 @@ __device__ __forceinline__ uint32_t ld_word_if(const uint8_t* p, bool pred, uint
 // and the underflow test, made once at the end of the stream (a refill read below the first data
 // word happened exactly when the cursor fell below first - 1).
 template <int V, int LK, bool BYPASS>
-__global__ void __maxnreg__(96) pop_bucket_kernel(const PopParams P) {
+__global__ void __maxnreg__(96) pop_bucket_kernel(const __grid_constant__ PopParams P) {
   using S = typename VT<V>::State;
   using W = typename VT<V>::Word;
   constexpr int TM = TM_BUCKET_GLOBAL;
@@ -447,7 +449,7 @@ __global__ void __maxnreg__(96) pop_bucket_kernel(const PopParams P) {
             }
             a = rown | ((((uint32_t)x) >> 1) & bmask);
           }
-          ov[q] = (int32_t)(sv + (uint32_t)ofs[q]);
+          ov[q] = (int32_t)sv;  // the table offset is added per chunk (rare steps return it added)
           en = ld_entry(a, pol_keep);  // every address is a row plus a masked offset: inside the table
           if (slow) {
             LeanState<V> st{x0, (S)w0, (long long)p0, err, 0};
@@ -456,10 +458,14 @@ __global__ void __maxnreg__(96) pop_bucket_kernel(const PopParams P) {
             nextw = (uint32_t)st.nextw;
             p = (int)min(max(st.p, -0x7fffffffll), 0x7fffffffll);
             err = st.err;
-            ov[q] = st.v;
+            ov[q] = (int32_t)((uint32_t)st.v - (uint32_t)ofs[q]);
             a = rown | ((((uint32_t)x) >> 1) & bmask);
             en = ld_entry(a, pol_keep);
           }
+        }
+        if (use_off) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) ov[q] = (int32_t)((uint32_t)ov[q] + (uint32_t)ofs[q]);
         }
         st_hint_v4(reinterpret_cast<int4*>(orow + 4 * (int64_t)c), make_int4(ov[0], ov[1], ov[2], ov[3]), pol_stream);
       }
