@@ -475,7 +475,7 @@ def _heavy_tail_case(rng, K=6, A=300, fp=16):
     return fp, cdfs, sizes, offs
 
 
-@pytest.mark.parametrize("kernel", ["lean", "fast"])
+@pytest.mark.parametrize("kernel", ["lean", "lean_l1", "fast"])
 @pytest.mark.parametrize("layout", ["bucket_global", "split_global", "split_smem", "fused_smem"])
 @pytest.mark.parametrize("lookup", ["search", "invcdf"])
 @pytest.mark.parametrize("variant", VARIANTS)
@@ -483,8 +483,13 @@ def test_pop_heavy_tails_and_overrun(C, kernel, layout, lookup, variant, monkeyp
     """Unit-frequency tails (bucket entries that cannot describe their cum range, so those steps
     take the split tables or the exact step), symbols drawn uniformly over the alphabet (every
     tail symbol occurs), bad table indexes in the pop, and pops that run past the encoded words
-    (underflow): outputs, final rows and error bits must all equal the oracle's."""
-    monkeypatch.setenv("TORCH_ANS_B200_POP_KERNEL", kernel)
+    (underflow): outputs, final rows and error bits must all equal the oracle's.  "lean" and
+    "lean_l1" run the lean kernels without and with the bucket layout's level-1 table in shared
+    memory."""
+    if kernel == "lean_l1" and layout != "bucket_global":
+        pytest.skip("the level-1 table fronts the bucket layout only")
+    monkeypatch.setenv("TORCH_ANS_B200_POP_KERNEL", "lean" if kernel.startswith("lean") else kernel)
+    monkeypatch.setenv("TORCH_ANS_B200_POP_L1", "1" if kernel == "lean_l1" else "0")
     monkeypatch.setenv("TORCH_ANS_B200_POP_LAYOUT", layout)
     rng = np.random.default_rng(zlib.crc32(f"tail-{kernel}-{layout}-{lookup}-{variant}".encode()))
     fp = 11 if layout.endswith("smem") else 16
@@ -513,17 +518,19 @@ def test_pop_heavy_tails_and_overrun(C, kernel, layout, lookup, variant, monkeyp
     assert same_rows(st.cpu().numpy(), ref_pop)
 
 
+@pytest.mark.parametrize("l1", ["0", "1"])
 @pytest.mark.parametrize("lookup", ["search", "invcdf"])
 @pytest.mark.parametrize("variant", VARIANTS)
-def test_bucket_pop_zero_offsets_tails_and_bad_rows(C, lookup, variant, monkeypatch):
+def test_bucket_pop_zero_offsets_tails_and_bad_rows(C, lookup, variant, l1, monkeypatch):
     """The bucket-layout pop with every table offset zero (the kernel then skips the per-step
     offset read), a table whose last symbol covers whole buckets up to 2^fp, unit-frequency tails
     (marker buckets), bad indexes and underflow: identical to the oracle.  Then rows whose length
     points past the row's end (a corrupted length the reference would read past the row for): the
     bucket pop must agree with the generic pop kernel, which takes the same exact step, and flag
-    underflow."""
+    underflow.  With and without the level-1 table in shared memory."""
     monkeypatch.setenv("TORCH_ANS_B200_POP_KERNEL", "lean")
     monkeypatch.setenv("TORCH_ANS_B200_POP_LAYOUT", "bucket_global")
+    monkeypatch.setenv("TORCH_ANS_B200_POP_L1", l1)
     rng = np.random.default_rng(zlib.crc32(f"bucket0-{lookup}-{variant}".encode()))
     fp = FP[variant]
     fp, cdfs, sizes, _ = _heavy_tail_case(rng, K=5, A=300, fp=fp)
@@ -571,15 +578,17 @@ def test_bucket_pop_zero_offsets_tails_and_bad_rows(C, lookup, variant, monkeypa
     assert np.array_equal(outs["lean"][0][1::4], sym[1::4])
 
 
+@pytest.mark.parametrize("l1", ["0", "1"])
 @pytest.mark.parametrize("lookup", ["search", "invcdf"])
 @pytest.mark.parametrize("variant", VARIANTS)
-def test_bucket_pop_secondary_table_overflow(C, lookup, variant, monkeypatch):
+def test_bucket_pop_secondary_table_overflow(C, lookup, variant, l1, monkeypatch):
     """Tables whose symbols alternate between frequency 1 and 2 over most of the range: nearly half
     of the buckets hold several symbols that are not a unit run, more than the secondary per-cum
     table has room for, so some of them decode from secondary blocks and the rest through the
-    exact step.  Both must give the oracle's bytes."""
+    exact step.  Both must give the oracle's bytes, with and without the level-1 table."""
     monkeypatch.setenv("TORCH_ANS_B200_POP_KERNEL", "lean")
     monkeypatch.setenv("TORCH_ANS_B200_POP_LAYOUT", "bucket_global")
+    monkeypatch.setenv("TORCH_ANS_B200_POP_L1", l1)
     rng = np.random.default_rng(zlib.crc32(f"secovf-{lookup}-{variant}".encode()))
     fp = FP[variant]
     A = 5000 if fp == 15 else 10000

@@ -160,6 +160,55 @@ __global__ void build_bucket_kernel(const int32_t* cdfs, int64_t ntables, int64_
   }
 }
 
+// Level-1 table for few streams per SM: one entry per 2^l1b cum values (l1b = kL1Bits), in the
+// bucket format, derived from the (exact) 16-cum entries: a coarse bucket is describable when its
+// fine entries all follow one two-symbol model -- a fine bucket before the boundary c1 repeats
+// (s0, c1, f0), the one holding c1 adds f1, one past it starts at c1 with symbol s0 + 1 and
+// freq f1 and holds no further boundary.  Anything else is a plain marker (the kernel then reads
+// the fine entry).
+__global__ void build_level1_kernel(const unsigned long long* BK, int64_t ntables, int fp, int l1b,
+                                    unsigned long long* L1) {
+  const int R = 1 << (l1b - kBucketBits);  // fine entries per coarse entry
+  const int64_t nb1 = (int64_t)1 << (fp - l1b), total = (ntables + 1) * nb1;
+  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t k = e / nb1;
+    unsigned long long out = 0xFFFFull;
+    if (k < ntables) {
+      const int64_t cb = e - k * nb1;
+      const unsigned long long* fe = BK + (k << (fp - kBucketBits)) + cb * R;
+      const uint32_t base = (uint32_t)(cb << l1b);
+      const unsigned long long e0 = fe[0];
+      const uint32_t s0 = (uint32_t)(e0 & 0xFFFFu), c1 = (uint32_t)((e0 >> 16) & 0xFFFFu) + 1u,
+                     f0 = (uint32_t)((e0 >> 32) & 0xFFFFu);
+      uint32_t f1 = 0;
+      bool seen1 = false, ok = s0 != 0xFFFFu;
+      for (int j = 0; ok && j < R; ++j) {
+        const unsigned long long ej = fe[j];
+        const uint32_t sj = (uint32_t)(ej & 0xFFFFu), c1j = (uint32_t)((ej >> 16) & 0xFFFFu) + 1u,
+                       f0j = (uint32_t)((ej >> 32) & 0xFFFFu), f1j = (uint32_t)(ej >> 48);
+        const uint32_t lj = base + ((uint32_t)j << kBucketBits), hj = lj + (1u << kBucketBits) - 1u;
+        if (sj == 0xFFFFu) {
+          ok = false;
+        } else if (hj < c1) {  // before the boundary
+          ok = sj == s0 && c1j == c1 && f0j == f0;
+        } else if (lj < c1) {  // holds the boundary
+          ok = sj == s0 && c1j == c1 && f0j == f0 && f1j != 0u && (!seen1 || f1j == f1);
+          f1 = f1j;
+          seen1 = true;
+        } else {  // past the boundary: symbol s0 + 1 from c1, no boundary of its own
+          ok = sj == s0 + 1u && c1j - f0j == c1 && c1j > hj && (!seen1 || f0j == f1);
+          f1 = f0j;
+          seen1 = true;
+        }
+      }
+      if (ok)
+        out = (unsigned long long)s0 | ((unsigned long long)(c1 - 1u) << 16) | ((unsigned long long)f0 << 32) |
+              ((unsigned long long)(seen1 ? f1 : 0u) << 48);
+    }
+    L1[e] = out;
+  }
+}
+
 __global__ void build_split_st_kernel(const int32_t* cdfs, int64_t ntables, int64_t cdf_width, int64_t st_stride,
                                       uint32_t* ST) {
   const int64_t total = ntables * st_stride;
@@ -408,6 +457,10 @@ static int64_t bucket_bytes(int64_t ntables, int fp) {
              ? (ntables + 2) * bucket_row_bytes(fp) + 256 + bucket_sec_cap(ntables, fp) * (8 << kBucketBits)
              : 0;
 }
+// level-1 table (ntables + 1 rows of 2^(fp - kL1Bits) entries), padded to 16 bytes
+static int64_t level1_bytes(int64_t ntables, int fp) {
+  return fp >= kL1Bits ? (((ntables + 1) * ((int64_t)8 << (fp - kL1Bits))) + 15) & ~(int64_t)15 : 0;
+}
 
 static bool tables_enabled() {
   const char* e = std::getenv("TORCH_ANS_B200_FUSED");
@@ -424,7 +477,8 @@ size_t pop_workspace_bytes(int variant, int lookup, int64_t ntables, int64_t cdf
     if (lookup != TANS_LOOKUP_ALIAS && split_bytes(lookup, ntables, cdf_width, fp) <= kSplitMaxBytes)
       extra = std::max(extra, align_up((size_t)(ntables << fp) * 2) +
                                   align_up((size_t)ntables * split_stride(lookup, cdf_width, fp) * 4) +
-                                  align_up((size_t)bucket_bytes(ntables, fp)));
+                                  align_up((size_t)bucket_bytes(ntables, fp)) +
+                                  align_up((size_t)level1_bytes(ntables, fp)));
     n += extra;
   }
   return n;
@@ -644,6 +698,15 @@ int pop_impl(int variant, int lookup, int interleave, int32_t* stream, int64_t b
       smem = (size_t)ring + (size_t)popf_table_smem(tm, ntables, fp, cdf_width, sstride);
     }
   }
+  // level-1 table in shared memory in front of the bucket table: for at most two streams per SM
+  // (one lane per warp, so a level-1 miss costs only its own lane) when it fits beside the records
+  bool use_l1 = false;
+  if (tm == TM_BUCKET_GLOBAL && lean && fp >= kL1Bits) {
+    const int env_l1 = env_int("TORCH_ANS_B200_POP_L1", -1);
+    const int64_t l1b = level1_bytes(ntables, fp);
+    use_l1 = (int64_t)smem + 16 + l1b <= kSmemBudget && (env_l1 == 1 || (env_l1 != 0 && batch <= 2 * (int64_t)dev_sms));
+    if (use_l1) smem += 16 + (size_t)l1b;
+  }
   const bool fast = tm >= 0;
   const bool need_fused = fast ? (tm == TM_FUSED_SMEM || tm == TM_FUSED_GLOBAL)
                                : (use_tables && ov != 100 && fused_bytes(ntables, fp) <= kFusedMaxBytes);
@@ -654,6 +717,7 @@ int pop_impl(int variant, int lookup, int interleave, int32_t* stream, int64_t b
   if (need_fused) need += align_up((size_t)(ntables << fp) * 4) + align_up((size_t)(ntables << fp) * 2);
   if (need_split) need += align_up((size_t)(ntables << fp) * 2) + align_up((size_t)ntables * sstride * 4);
   if (need_bucket) need += align_up((size_t)bucket_bytes(ntables, fp));
+  if (use_l1) need += align_up((size_t)level1_bytes(ntables, fp));
   void* ws = workspace;
   bool owned = false;
   if (!ws) {
@@ -698,6 +762,11 @@ int pop_impl(int variant, int lookup, int interleave, int32_t* stream, int64_t b
       char* after = reinterpret_cast<char*>(const_cast<unsigned long long*>(P.fBK)) + (ntables + 1) * rb;
       P.fSEC = reinterpret_cast<unsigned long long*>(after + 256);
       P.sec_cap = bucket_sec_cap(ntables, fp);
+      wsp += align_up((size_t)bucket_bytes(ntables, fp));
+      if (use_l1) {
+        P.fL1 = reinterpret_cast<unsigned long long*>(wsp);
+        P.l1_bytes = level1_bytes(ntables, fp);
+      }
     }
   }
   {
@@ -730,6 +799,12 @@ int pop_impl(int variant, int lookup, int interleave, int32_t* stream, int64_t b
       if (variant == TANS_RANS64) build_bucket_kernel<0, LK_SEARCH><<<bb, 128, 0, s>>>(cdfs, ntables, cdf_width, tinfo, fp, BK, SEC, sc, cnt);
       else if (variant == TANS_RANS32) build_bucket_kernel<1, LK_SEARCH><<<bb, 128, 0, s>>>(cdfs, ntables, cdf_width, tinfo, fp, BK, SEC, sc, cnt);
       else build_bucket_kernel<2, LK_SEARCH><<<bb, 128, 0, s>>>(cdfs, ntables, cdf_width, tinfo, fp, BK, SEC, sc, cnt);
+    }
+    if (use_l1) {
+      const int64_t n1 = (ntables + 1) << (fp - kL1Bits);
+      const int b1 = (int)std::max<int64_t>(1, std::min<int64_t>((n1 + 127) / 128, 16 * (int64_t)dev_sms));
+      build_level1_kernel<<<b1, 128, 0, s>>>(BK, ntables, fp, kL1Bits, const_cast<unsigned long long*>(P.fL1));
+      note_launch();
     }
   }
   if (fast) {

@@ -30,6 +30,8 @@ struct PopParams {
   const unsigned long long* fBK;  // bucket layout: one entry per 16 cum values
   const unsigned long long* fSEC; // bucket layout: per-cum blocks of marker buckets (type 2)
   int64_t sec_cap;                // blocks the secondary table holds
+  const unsigned long long* fL1;  // bucket layout: level-1 table staged in shared memory (or null)
+  int64_t l1_bytes;               // its bytes (a multiple of 16; 0: no level-1 table)
   int spt;             // streams per thread (fast kernel)
   int fused_smem;      // fused table staged in shared memory
   int tin_smem;        // per-table info staged in shared memory

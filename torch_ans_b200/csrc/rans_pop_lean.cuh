@@ -267,6 +267,12 @@ __device__ __forceinline__ unsigned long long ld_entry(uintptr_t a, unsigned lon
   asm volatile("ld.global.nc.L2::cache_hint.u64 %0, [%1], %2;\n" : "=l"(v) : "l"(a), "l"(policy));
   return v;
 }
+// the same from a 32-bit shared-memory address (the level-1 table)
+__device__ __forceinline__ unsigned long long ld_entry_shared(uint32_t a) {
+  unsigned long long v;
+  asm volatile("ld.shared.u64 %0, [%1];\n" : "=l"(v) : "r"(a));
+  return v;
+}
 
 // Stream word at p when `pred`, else `w` (a predicated load, zero-extended: no branch on the
 // serial step)
@@ -310,7 +316,7 @@ __device__ __forceinline__ uint32_t ld_word_if(const uint8_t* p, bool pred, uint
 // index loads two chunks ahead, the predicated prefetch of the next stream word,
 // and the underflow test, made once at the end of the stream (a refill read below the first data
 // word happened exactly when the cursor fell below first - 1).
-template <int V, int LK, bool BYPASS>
+template <int V, int LK, bool BYPASS, bool L1>
 __global__ void __maxnreg__(96) pop_bucket_kernel(const __grid_constant__ PopParams P) {
   using S = typename VT<V>::State;
   using W = typename VT<V>::Word;
@@ -322,6 +328,15 @@ __global__ void __maxnreg__(96) pop_bucket_kernel(const __grid_constant__ PopPar
   // row (the shared region holds 32 bytes per table, these use 24 + 8)
   TableInfo* tsm = reinterpret_cast<TableInfo*>(smem_raw);
   int2* tsm2 = reinterpret_cast<int2*>(tsm + P.ntables);
+  // level-1 table (L1): one entry per 2^kL1Bits cum values, copied in by the whole block
+  unsigned char* l1s = popf_align16(smem_raw + P.ntables * 32);
+  if constexpr (L1) {
+    const uint4* src = reinterpret_cast<const uint4*>(P.fL1);
+    uint4* dst = reinterpret_cast<uint4*>(l1s);
+    const int64_t n16 = P.l1_bytes >> 4;
+#pragma unroll 4
+    for (int64_t i = tid; i < n16; i += T) dst[i] = __ldg(src + i);
+  }
   int any_off = 0;
   for (int64_t k = tid; k < P.ntables; k += T) {
     const TableInfo ti = P.tinfo[k];
@@ -359,6 +374,23 @@ __global__ void __maxnreg__(96) pop_bucket_kernel(const __grid_constant__ PopPar
   const uint32_t kmark = (uint32_t)P.ntables;
   const uint32_t rowbytes = 1u << (P.fp - 1);
   const uintptr_t bk0 = reinterpret_cast<uintptr_t>(P.fBK);
+  // entry addresses: the bucket table's row of table k, or with L1 the level-1 row in shared
+  // memory (a 32-bit shared address), plus the entry's byte offset taken from the state's low word
+  const uint32_t l1base = smem_u32(l1s);
+  const uint32_t l1rowbytes = 8u << (P.fp - kL1Bits);
+  const uint32_t l1mask = (cmask >> kL1Bits) << 3;
+  auto row_of = [&](int32_t k) -> uintptr_t {
+    if constexpr (L1) return (uintptr_t)(l1base + min((uint32_t)k, kmark) * l1rowbytes);
+    else return bk0 + (uintptr_t)min((uint32_t)k, kmark) * rowbytes;
+  };
+  auto addr_of = [&](uintptr_t rowp, uint32_t lowword) -> uintptr_t {
+    if constexpr (L1) return rowp + ((lowword >> (kL1Bits - 3)) & l1mask);
+    else return rowp | ((lowword >> 1) & bmask);
+  };
+  auto load_at = [&](uintptr_t at) -> unsigned long long {
+    if constexpr (L1) return ld_entry_shared((uint32_t)at);
+    else return ld_entry(at, pol_keep);
+  };
   const int64_t N = P.nsym;
   const int nch = (int)(N >> 2);
   const int32_t* irow = P.idx + b * N;
@@ -385,10 +417,10 @@ __global__ void __maxnreg__(96) pop_bucket_kernel(const __grid_constant__ PopPar
     // kn0 = kn1 reads a load issued a whole chunk earlier)
     int4 kn0 = nch > 0 ? ld_idx4(irow, pol_stream) : make_int4(0, 0, 0, 0);
     int4 kn1 = nch > 1 ? ld_idx4(irow + 4, pol_stream) : make_int4(0, 0, 0, 0);
-    uintptr_t a = (bk0 + (uintptr_t)min((uint32_t)kn0.x, kmark) * rowbytes) | ((((uint32_t)x) >> 1) & bmask);
+    uintptr_t a = addr_of(row_of(kn0.x), (uint32_t)x);
     // the entry of the next step: each step issues the next step's load before its own rare-step
     // branch, so the branch resolves while the load is in flight (the rare step reissues it)
-    unsigned long long en = ld_entry(a, pol_keep);
+    unsigned long long en = load_at(a);
 #pragma unroll 1
     for (int c = 0; c < nch; ++c) {
       {
@@ -412,7 +444,7 @@ __global__ void __maxnreg__(96) pop_bucket_kernel(const __grid_constant__ PopPar
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
           const int32_t k = kv[q];
-          const uintptr_t rown = bk0 + (uintptr_t)min((uint32_t)kv[q + 1], kmark) * rowbytes;
+          const uintptr_t rown = row_of(kv[q + 1]);
           const S x0 = x;
           const uint32_t w0 = nextw;
           const int p0 = p;
@@ -432,8 +464,8 @@ __global__ void __maxnreg__(96) pop_bucket_kernel(const __grid_constant__ PopPar
           if constexpr (!VT<V>::LOOP) {
             // single refill (rans64, rans32_16): the low word after a refill is the prefetched word
             const bool r = (unsigned long long)x < VT<V>::LB;
-            const uintptr_t an = rown | ((((uint32_t)x) >> 1) & bmask);
-            const uintptr_t ar = rown | ((nextw >> 1) & bmask);
+            const uintptr_t an = addr_of(rown, (uint32_t)x);
+            const uintptr_t ar = addr_of(rown, nextw);
             x = r ? (S)((x << VT<V>::WB) | (S)nextw) : x;
             a = r ? ar : an;
             p -= r ? 1 : 0;
@@ -447,20 +479,57 @@ __global__ void __maxnreg__(96) pop_bucket_kernel(const __grid_constant__ PopPar
               p -= r ? 1 : 0;
               nextw = ld_word_if(pw + p, r && !slow && p >= first, r ? 0u : nextw);
             }
-            a = rown | ((((uint32_t)x) >> 1) & bmask);
+            a = addr_of(rown, (uint32_t)x);
           }
           ov[q] = (int32_t)sv;  // the table offset is added per chunk (rare steps return it added)
-          en = ld_entry(a, pol_keep);  // every address is a row plus a masked offset: inside the table
+          en = load_at(a);  // every address is a row plus a masked offset: inside the table
           if (slow) {
-            LeanState<V> st{x0, (S)w0, (long long)p0, err, 0};
-            st = popb_rare<V, LK, BYPASS>(P, st, row, k, e, tsm);
-            x = st.x;
-            nextw = (uint32_t)st.nextw;
-            p = (int)min(max(st.p, -0x7fffffffll), 0x7fffffffll);
-            err = st.err;
-            ov[q] = (int32_t)((uint32_t)st.v - (uint32_t)ofs[q]);
-            a = rown | ((((uint32_t)x) >> 1) & bmask);
-            en = ld_entry(a, pol_keep);
+            bool done = false;
+            unsigned long long er = e;  // the entry the rare step decodes
+            if constexpr (L1) {
+              // the level-1 entry could not decode this cum: the 16-cum entry from the bucket table
+              const uintptr_t rk = bk0 + (uintptr_t)min((uint32_t)k, kmark) * rowbytes;
+              er = ld_hint_u64(reinterpret_cast<const unsigned long long*>(rk | ((((uint32_t)x0) >> 1) & bmask)),
+                               pol_keep);
+              const uint32_t c0 = (uint32_t)x0 & cmask;
+              const uint32_t lo2 = (uint32_t)er, hi2 = (uint32_t)(er >> 32);
+              const bool up2 = (c0 << 16) > lo2;
+              const uint32_t g0 = hi2 & 0xFFFFu;
+              const uint32_t f2 = up2 ? (hi2 >> 16) : g0;
+              const uint32_t off2 = (c0 - 1u - (lo2 >> 16)) + (up2 ? 0u : g0);
+              const uint32_t s2 = lo2 & 0xFFFFu;
+              const uint32_t sv2 = s2 + (up2 ? 1u : 0u);
+              bool slow2 = s2 == 0xFFFFu;
+              if constexpr (BYPASS) slow2 |= (int32_t)sv2 == esc[q];
+              if (!slow2) {
+                S xx = (S)((x0 >> P.fp) * (S)f2 + (S)off2);
+                uint32_t ww = w0;
+                int pp = p0;
+#pragma unroll
+                for (int t = 0; t < VT<V>::MAX_RENORM; ++t) {
+                  const bool r = (unsigned long long)xx < VT<V>::LB;
+                  xx = r ? (S)((xx << VT<V>::WB) | (S)ww) : xx;
+                  pp -= r ? 1 : 0;
+                  ww = ld_word_if(pw + pp, r && pp >= first, r ? 0u : ww);
+                }
+                x = xx;
+                nextw = ww;
+                p = pp;
+                ov[q] = (int32_t)sv2;
+                done = true;
+              }
+            }
+            if (!done) {
+              LeanState<V> st{x0, (S)w0, (long long)p0, err, 0};
+              st = popb_rare<V, LK, BYPASS>(P, st, row, k, er, tsm);
+              x = st.x;
+              nextw = (uint32_t)st.nextw;
+              p = (int)min(max(st.p, -0x7fffffffll), 0x7fffffffll);
+              err = st.err;
+              ov[q] = (int32_t)((uint32_t)st.v - (uint32_t)ofs[q]);
+            }
+            a = addr_of(rown, (uint32_t)x);
+            en = load_at(a);
           }
         }
         if (use_off) {
@@ -481,12 +550,17 @@ template <int V>
 bool launch_pop_lean(const PopParams& P, int lookup, bool bypass, int tm, int blocks, int threads, size_t smem,
                      cudaStream_t s);
 
+template <int V, int LK, bool BY, bool L1>
+void popb_go1(const PopParams& P, int blocks, int threads, size_t smem, cudaStream_t s) {
+  if (smem > 48 * 1024)
+    cudaFuncSetAttribute(pop_bucket_kernel<V, LK, BY, L1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  pop_bucket_kernel<V, LK, BY, L1><<<blocks, threads, smem, s>>>(P);
+  note_launch();
+}
 template <int V, int LK, bool BY>
 void popb_go(const PopParams& P, int blocks, int threads, size_t smem, cudaStream_t s) {
-  if (smem > 48 * 1024)
-    cudaFuncSetAttribute(pop_bucket_kernel<V, LK, BY>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  pop_bucket_kernel<V, LK, BY><<<blocks, threads, smem, s>>>(P);
-  note_launch();
+  if (P.fL1 && P.l1_bytes > 0) popb_go1<V, LK, BY, true>(P, blocks, threads, smem, s);
+  else popb_go1<V, LK, BY, false>(P, blocks, threads, smem, s);
 }
 
 template <int V, int LK, bool BY, int TM>
