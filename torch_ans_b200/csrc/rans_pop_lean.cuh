@@ -1,17 +1,18 @@
-// rans_pop_lean.cuh -- single-state pop with the shortest serial step (rows 16-byte aligned,
-// length % 4 == 0).
+// rans_pop_lean.cuh -- single-state pops with the shortest serial step, one thread per stream
+// (rows 16-byte aligned, length % 4 == 0).
 //
 // A pop is one serial chain per stream (rans_utils.hpp:379-532 per symbol); with one thread per
-// stream, its speed is the latency of one step.  The step here keeps on that chain only
-//   cum = x mod 2^fp -> table load -> (symbol, start, freq) -> x = freq * (x >> fp) + cum - start
-//   -> refill with the word prefetched into a register,
-// and everything else off it: table indexes arrive as 16-byte loads four chunks ahead, the table row
-// of each step is computed from its index while the previous step's table load is in flight, the
-// symbol's output offset and escape slot come from shared memory, and the four symbols of a chunk
-// leave as one 16-byte store.  Steps the straight-line code cannot do exactly (an index outside the
-// table list, a table entry marked as not describable, an escape, a row whose length points outside
-// it) take the reference-exact step on their own lane; underflow needs no special case (a word
-// outside the row reads as 0 and sets TANS_DEV_UNDERFLOW, as the exact step does).
+// stream, its speed is the latency of one step.  Two kernels:
+//   pop_lean_kernel   the split and fused layouts: cum -> table load(s) -> (symbol, start, freq)
+//                     -> x = freq * (x >> fp) + cum - start -> refill with the word prefetched
+//                     into a register; table indexes arrive four chunks ahead, offsets and escape
+//                     slots come from shared memory, four symbols leave as one 16-byte store;
+//   pop_bucket_kernel the bucket layout (and its level-1 table in shared memory), described above
+//                     the kernel.
+// Steps the straight-line code cannot do exactly (an index outside the table list, a table entry
+// marked as not describable, an escape, a row whose length points outside it) take the
+// reference-exact step out of line on their own lane; a word outside the row reads as 0 and sets
+// TANS_DEV_UNDERFLOW, as the exact step does.
 //
 // Table layouts are those of the fast kernel (built per call by replaying the reference lookup).
 #pragma once
@@ -295,7 +296,11 @@ __device__ __forceinline__ uint32_t ld_word_if(const uint8_t* p, bool pred, uint
   return w;
 }
 
-// Pop over the bucket layout (TM_BUCKET_GLOBAL): one dependent L2 load per step.
+// Pop over the bucket layout (TM_BUCKET_GLOBAL): one dependent L2 load per step, or with L1 one
+// dependent shared-memory load (the level-1 table: the same entry format over 256 cum values,
+// copied into each block; its markers read the 16-cum entry from L2 in the rare branch, then the
+// rare step if that is a marker too).  L1 is chosen for at most two streams per SM, where every
+// stream has its own warp and a level-1 miss delays only its own lane.
 //
 // Entry of 16 cum values (built per call, every cum checked against the reference lookup):
 //   lo = s0 | (c1 - 1) << 16,  hi = f0 | f1 << 16
