@@ -274,6 +274,15 @@ __device__ __forceinline__ unsigned long long ld_entry_shared(uint32_t a) {
   asm volatile("ld.shared.u64 %0, [%1];\n" : "=l"(v) : "r"(a));
   return v;
 }
+// the fused layout's two entries of index i (D: (freq - 1) | offset << 16, S: the symbol) from
+// shared memory, as D | S << 32
+__device__ __forceinline__ unsigned long long ld_fused_shared(uint32_t dbase, uint32_t sbase, uint32_t i) {
+  uint32_t d, s;
+  asm volatile("ld.shared.u32 %0, [%2];\n ld.shared.u16 %1, [%3];\n"
+               : "=r"(d), "=r"(s)
+               : "r"(dbase + 4u * i), "r"(sbase + 2u * i));
+  return (unsigned long long)d | ((unsigned long long)s << 32);
+}
 
 // Stream word at p when `pred`, else `w` (a predicated load, zero-extended: no branch on the
 // serial step)
@@ -321,11 +330,16 @@ __device__ __forceinline__ uint32_t ld_word_if(const uint8_t* p, bool pred, uint
 // index loads two chunks ahead, the predicated prefetch of the next stream word,
 // and the underflow test, made once at the end of the stream (a refill read below the first data
 // word happened exactly when the cursor fell below first - 1).
-template <int V, int LK, bool BYPASS, bool L1>
+// table modes of pop_bucket_kernel
+enum : int { BM_L2 = 0, BM_L1 = 1, BM_FUSED = 2 };
+
+template <int V, int LK, bool BYPASS, int MODE>
 __global__ void __maxnreg__(96) pop_bucket_kernel(const __grid_constant__ PopParams P) {
   using S = typename VT<V>::State;
   using W = typename VT<V>::Word;
-  constexpr int TM = TM_BUCKET_GLOBAL;
+  constexpr bool L1 = MODE == BM_L1;
+  constexpr bool FUSED = MODE == BM_FUSED;
+  constexpr int TM = FUSED ? TM_FUSED_SMEM : TM_BUCKET_GLOBAL;
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const int T = blockDim.x, tid = threadIdx.x;
   const int warps = T >> 5, warp = tid >> 5, lane = tid & 31;
@@ -333,8 +347,15 @@ __global__ void __maxnreg__(96) pop_bucket_kernel(const __grid_constant__ PopPar
   // row (the shared region holds 32 bytes per table, these use 24 + 8)
   TableInfo* tsm = reinterpret_cast<TableInfo*>(smem_raw);
   int2* tsm2 = reinterpret_cast<int2*>(tsm + P.ntables);
-  // level-1 table (L1): one entry per 2^kL1Bits cum values, copied in by the whole block
+  // level-1 table (L1): one entry per 2^kL1Bits cum values, copied in by the whole block; or
+  // (FUSED) the fused D and S tables of every table, staged by bulk copies
   unsigned char* l1s = popf_align16(smem_raw + P.ntables * 32);
+  const int64_t m = P.ntables << P.fp;
+  uint32_t* tD = reinterpret_cast<uint32_t*>(l1s);
+  uint16_t* tS = reinterpret_cast<uint16_t*>(l1s + ((m * 4 + 15) & ~(int64_t)15));
+  __shared__ unsigned long long stage_bar;
+  __shared__ int stage_tma;
+  if constexpr (FUSED) popf_stage_begin<TM_FUSED_SMEM>(P, tD, tS, m, &stage_bar, &stage_tma);
   if constexpr (L1) {
     const uint4* src = reinterpret_cast<const uint4*>(P.fL1);
     uint4* dst = reinterpret_cast<uint4*>(l1s);
@@ -350,7 +371,13 @@ __global__ void __maxnreg__(96) pop_bucket_kernel(const __grid_constant__ PopPar
     any_off |= ti.offset != 0 ? 1 : 0;
   }
   if (tid == 0) tsm2[P.ntables] = make_int2(0, -1);
+  bool staged = true;
+  if constexpr (FUSED) staged = popf_stage_end<TM_FUSED_SMEM>(&stage_bar, &stage_tma);
   const bool use_off = __syncthreads_or(any_off) != 0;
+  if (!staged) {
+    if (tid == 0) report(P.status, DEV_STALLED);
+    return;
+  }
   if (lane >= P.lanes) return;
   const int64_t b = ((int64_t)blockIdx.x * warps + warp) * P.lanes + lane;
   if (b >= P.batch) return;
@@ -384,16 +411,23 @@ __global__ void __maxnreg__(96) pop_bucket_kernel(const __grid_constant__ PopPar
   const uint32_t l1base = smem_u32(l1s);
   const uint32_t l1rowbytes = 8u << (P.fp - kL1Bits);
   const uint32_t l1mask = (cmask >> kL1Bits) << 3;
+  // FUSED: entry index (k << fp) | cum into the shared D and S tables; a table index outside the
+  // list reads table 0 and is flagged separately (the fused tables have no marker row)
+  const uint32_t fdbase = smem_u32(tD), fsbase = smem_u32(tS);
+  const uint32_t klast = (uint32_t)(P.ntables - 1);
   auto row_of = [&](int32_t k) -> uintptr_t {
     if constexpr (L1) return (uintptr_t)(l1base + min((uint32_t)k, kmark) * l1rowbytes);
+    else if constexpr (FUSED) return (uintptr_t)(((uint32_t)k <= klast ? (uint32_t)k : 0u) << P.fp);
     else return bk0 + (uintptr_t)min((uint32_t)k, kmark) * rowbytes;
   };
   auto addr_of = [&](uintptr_t rowp, uint32_t lowword) -> uintptr_t {
     if constexpr (L1) return rowp + ((lowword >> (kL1Bits - 3)) & l1mask);
+    else if constexpr (FUSED) return rowp + (lowword & cmask);
     else return rowp | ((lowword >> 1) & bmask);
   };
   auto load_at = [&](uintptr_t at) -> unsigned long long {
     if constexpr (L1) return ld_entry_shared((uint32_t)at);
+    else if constexpr (FUSED) return ld_fused_shared(fdbase, fsbase, (uint32_t)at);
     else return ld_entry(at, pol_keep);
   };
   const int64_t N = P.nsym;
@@ -408,7 +442,7 @@ __global__ void __maxnreg__(96) pop_bucket_kernel(const __grid_constant__ PopPar
 #pragma unroll 1
       for (int q = 0; q < 4; ++q) {
         LeanState<V> st{x, (S)nextw, (long long)p, err, 0};
-        st = popl_exact<V, LK, BYPASS, TM>(P, st, row, irow[4 * (int64_t)c + q], tsm, nullptr, nullptr);
+        st = popl_exact<V, LK, BYPASS, TM>(P, st, row, irow[4 * (int64_t)c + q], tsm, tD, tS);
         x = st.x;
         nextw = (uint32_t)st.nextw;
         p = (int)min(max(st.p, -0x7fffffffll), 0x7fffffffll);
@@ -457,13 +491,22 @@ __global__ void __maxnreg__(96) pop_bucket_kernel(const __grid_constant__ PopPar
           const uint32_t cum = (uint32_t)x & cmask;
           const S xs = x >> P.fp;
           const uint32_t lo = (uint32_t)e, hi = (uint32_t)(e >> 32);
-          const bool up = (cum << 16) > lo;  // cum >= c1
-          const uint32_t f0 = hi & 0xFFFFu;
-          const uint32_t f = up ? (hi >> 16) : f0;
-          const uint32_t off = (cum - 1u - (lo >> 16)) + (up ? 0u : f0);
-          const uint32_t s0 = lo & 0xFFFFu;
-          const uint32_t sv = s0 + (up ? 1u : 0u);
-          bool slow = s0 == 0xFFFFu;
+          uint32_t f, off, sv;
+          bool slow;
+          if constexpr (FUSED) {
+            f = (lo & 0xFFFFu) + 1u;
+            off = lo >> 16;
+            sv = hi;
+            slow = hi == 0xFFFFu || (uint32_t)k > klast;
+          } else {
+            const bool up = (cum << 16) > lo;  // cum >= c1
+            const uint32_t f0 = hi & 0xFFFFu;
+            f = up ? (hi >> 16) : f0;
+            off = (cum - 1u - (lo >> 16)) + (up ? 0u : f0);
+            const uint32_t s0 = lo & 0xFFFFu;
+            sv = s0 + (up ? 1u : 0u);
+            slow = s0 == 0xFFFFu;
+          }
           if constexpr (BYPASS) slow |= (int32_t)sv == esc[q];
           x = (S)(xs * (S)f + (S)off);
           if constexpr (!VT<V>::LOOP) {
@@ -526,7 +569,8 @@ __global__ void __maxnreg__(96) pop_bucket_kernel(const __grid_constant__ PopPar
             }
             if (!done) {
               LeanState<V> st{x0, (S)w0, (long long)p0, err, 0};
-              st = popb_rare<V, LK, BYPASS>(P, st, row, k, er, tsm);
+              if constexpr (FUSED) st = popl_exact<V, LK, BYPASS, TM_FUSED_SMEM>(P, st, row, k, tsm, tD, tS);
+              else st = popb_rare<V, LK, BYPASS>(P, st, row, k, er, tsm);
               x = st.x;
               nextw = (uint32_t)st.nextw;
               p = (int)min(max(st.p, -0x7fffffffll), 0x7fffffffll);
@@ -555,17 +599,17 @@ template <int V>
 bool launch_pop_lean(const PopParams& P, int lookup, bool bypass, int tm, int blocks, int threads, size_t smem,
                      cudaStream_t s);
 
-template <int V, int LK, bool BY, bool L1>
+template <int V, int LK, bool BY, int MODE>
 void popb_go1(const PopParams& P, int blocks, int threads, size_t smem, cudaStream_t s) {
   if (smem > 48 * 1024)
-    cudaFuncSetAttribute(pop_bucket_kernel<V, LK, BY, L1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  pop_bucket_kernel<V, LK, BY, L1><<<blocks, threads, smem, s>>>(P);
+    cudaFuncSetAttribute(pop_bucket_kernel<V, LK, BY, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  pop_bucket_kernel<V, LK, BY, MODE><<<blocks, threads, smem, s>>>(P);
   note_launch();
 }
 template <int V, int LK, bool BY>
 void popb_go(const PopParams& P, int blocks, int threads, size_t smem, cudaStream_t s) {
-  if (P.fL1 && P.l1_bytes > 0) popb_go1<V, LK, BY, true>(P, blocks, threads, smem, s);
-  else popb_go1<V, LK, BY, false>(P, blocks, threads, smem, s);
+  if (P.fL1 && P.l1_bytes > 0) popb_go1<V, LK, BY, BM_L1>(P, blocks, threads, smem, s);
+  else popb_go1<V, LK, BY, BM_L2>(P, blocks, threads, smem, s);
 }
 
 template <int V, int LK, bool BY, int TM>
@@ -579,21 +623,21 @@ void popl_go(const PopParams& P, int blocks, int threads, size_t smem, cudaStrea
 template <int V, bool BY>
 bool popl_tm(const PopParams& P, int lookup, int tm, int blocks, int threads, size_t smem, cudaStream_t s) {
   if (lookup == 2) {  // alias: only the fused layout (its offsets depend on cum, not on s)
-    if (tm == TM_FUSED_SMEM) popl_go<V, 2, BY, TM_FUSED_SMEM>(P, blocks, threads, smem, s);
+    if (tm == TM_FUSED_SMEM) popb_go1<V, 2, BY, BM_FUSED>(P, blocks, threads, smem, s);
     else if (tm == TM_FUSED_GLOBAL) popl_go<V, 2, BY, TM_FUSED_GLOBAL>(P, blocks, threads, smem, s);
     else return false;
     return true;
   }
   if (lookup == 1) {
     if (tm == TM_BUCKET_GLOBAL) popb_go<V, 1, BY>(P, blocks, threads, smem, s);
-    else if (tm == TM_FUSED_SMEM) popl_go<V, 1, BY, TM_FUSED_SMEM>(P, blocks, threads, smem, s);
+    else if (tm == TM_FUSED_SMEM) popb_go1<V, 1, BY, BM_FUSED>(P, blocks, threads, smem, s);
     else if (tm == TM_SPLIT_SMEM) popl_go<V, 1, BY, TM_SPLIT_SMEM>(P, blocks, threads, smem, s);
     else if (tm == TM_SPLIT_GLOBAL) popl_go<V, 1, BY, TM_SPLIT_GLOBAL>(P, blocks, threads, smem, s);
     else return false;
     return true;
   }
   if (tm == TM_BUCKET_GLOBAL) popb_go<V, 0, BY>(P, blocks, threads, smem, s);
-  else if (tm == TM_FUSED_SMEM) popl_go<V, 0, BY, TM_FUSED_SMEM>(P, blocks, threads, smem, s);
+  else if (tm == TM_FUSED_SMEM) popb_go1<V, 0, BY, BM_FUSED>(P, blocks, threads, smem, s);
   else if (tm == TM_SPLIT_SMEM) popl_go<V, 0, BY, TM_SPLIT_SMEM>(P, blocks, threads, smem, s);
   else if (tm == TM_SPLIT_GLOBAL) popl_go<V, 0, BY, TM_SPLIT_GLOBAL>(P, blocks, threads, smem, s);
   else return false;
