@@ -54,7 +54,7 @@ def parse():
     ap.add_argument("--scale", type=float, default=1.0, help="fraction of the configuration's streams")
     ap.add_argument("--length-scale", type=float, default=1.0, help="fraction of the configuration's stream length")
     ap.add_argument("--e2e-steps", type=int, default=2)
-    ap.add_argument("--e2e-chunk", type=int, default=16384, help="symbols per column chunk of the host pipeline")
+    ap.add_argument("--e2e-chunk", type=int, default=4096, help="symbols per column chunk of the host pipeline")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="target CPU work of the baseline sample")
