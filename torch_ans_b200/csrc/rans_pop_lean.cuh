@@ -534,12 +534,29 @@ __global__ void __maxnreg__(96) pop_bucket_kernel(const __grid_constant__ PopPar
           if (slow) {
             bool done = false;
             unsigned long long er = e;  // the entry the rare step decodes
+            const uint32_t c0 = (uint32_t)x0 & cmask;
+            // finish the step from the saved state with x already decoded (before renormalisation)
+            auto finish = [&](S xx, uint32_t svv) {
+              uint32_t ww = w0;
+              int pp = p0;
+#pragma unroll
+              for (int t = 0; t < VT<V>::MAX_RENORM; ++t) {
+                const bool r = (unsigned long long)xx < VT<V>::LB;
+                xx = r ? (S)((xx << VT<V>::WB) | (S)ww) : xx;
+                pp -= r ? 1 : 0;
+                ww = ld_word_if(pw + pp, r && pp >= first, r ? 0u : ww);
+              }
+              x = xx;
+              nextw = ww;
+              p = pp;
+              ov[q] = (int32_t)svv;
+              done = true;
+            };
             if constexpr (L1) {
               // the level-1 entry could not decode this cum: the 16-cum entry from the bucket table
               const uintptr_t rk = bk0 + (uintptr_t)min((uint32_t)k, kmark) * rowbytes;
               er = ld_hint_u64(reinterpret_cast<const unsigned long long*>(rk | ((((uint32_t)x0) >> 1) & bmask)),
                                pol_keep);
-              const uint32_t c0 = (uint32_t)x0 & cmask;
               const uint32_t lo2 = (uint32_t)er, hi2 = (uint32_t)(er >> 32);
               const bool up2 = (c0 << 16) > lo2;
               const uint32_t g0 = hi2 & 0xFFFFu;
@@ -549,22 +566,14 @@ __global__ void __maxnreg__(96) pop_bucket_kernel(const __grid_constant__ PopPar
               const uint32_t sv2 = s2 + (up2 ? 1u : 0u);
               bool slow2 = s2 == 0xFFFFu;
               if constexpr (BYPASS) slow2 |= (int32_t)sv2 == esc[q];
-              if (!slow2) {
-                S xx = (S)((x0 >> P.fp) * (S)f2 + (S)off2);
-                uint32_t ww = w0;
-                int pp = p0;
-#pragma unroll
-                for (int t = 0; t < VT<V>::MAX_RENORM; ++t) {
-                  const bool r = (unsigned long long)xx < VT<V>::LB;
-                  xx = r ? (S)((xx << VT<V>::WB) | (S)ww) : xx;
-                  pp -= r ? 1 : 0;
-                  ww = ld_word_if(pw + pp, r && pp >= first, r ? 0u : ww);
-                }
-                x = xx;
-                nextw = ww;
-                p = pp;
-                ov[q] = (int32_t)sv2;
-                done = true;
+              if (!slow2) finish((S)((x0 >> P.fp) * (S)f2 + (S)off2), sv2);
+            }
+            if constexpr (!FUSED) {
+              // a run of unit-frequency symbols (type-1 marker): symbol cum + d, freq 1, offset 0,
+              // decoded here without the call (the most common marker)
+              if (!done && (er & 0x3FFFFull) == 0x1FFFFull) {
+                const uint32_t svu = c0 + (uint32_t)(er >> 32);
+                if (!BYPASS || (int32_t)svu != esc[q]) finish((S)(x0 >> P.fp), svu);
               }
             }
             if (!done) {
