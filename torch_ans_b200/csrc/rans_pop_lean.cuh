@@ -569,11 +569,18 @@ __global__ void __maxnreg__(96) pop_bucket_kernel(const __grid_constant__ PopPar
               if (!slow2) finish((S)((x0 >> P.fp) * (S)f2 + (S)off2), sv2);
             }
             if constexpr (!FUSED) {
-              // a run of unit-frequency symbols (type-1 marker): symbol cum + d, freq 1, offset 0,
-              // decoded here without the call (the most common marker)
+              // the typed markers, decoded here without the call: a run of unit-frequency symbols
+              // (type 1: symbol cum + d, freq 1, offset 0) or a block of per-cum entries in the
+              // secondary table (type 2: s | offset << 16 | freq << 32, one load)
               if (!done && (er & 0x3FFFFull) == 0x1FFFFull) {
                 const uint32_t svu = c0 + (uint32_t)(er >> 32);
                 if (!BYPASS || (int32_t)svu != esc[q]) finish((S)(x0 >> P.fp), svu);
+              } else if (!done && (er & 0x3FFFFull) == 0x2FFFFull) {
+                const unsigned long long d2 =
+                    ld_hint_u64(P.fSEC + ((er >> 18) << kBucketBits) + (c0 & ((1u << kBucketBits) - 1u)), pol_keep);
+                const uint32_t svs = (uint32_t)(d2 & 0xFFFFull);
+                if (!BYPASS || (int32_t)svs != esc[q])
+                  finish((S)((x0 >> P.fp) * (S)(uint32_t)(d2 >> 32) + (S)((uint32_t)(d2 >> 16) & 0xFFFFu)), svs);
               }
             }
             if (!done) {
