@@ -517,7 +517,9 @@ __global__ void __maxnreg__(96) pop_bucket_kernel(const __grid_constant__ PopPar
             x = r ? (S)((x << VT<V>::WB) | (S)nextw) : x;
             a = r ? ar : an;
             p -= r ? 1 : 0;
-            nextw = ld_word_if(pw + p, r && !slow && p >= first, r ? 0u : nextw);
+            // (on a slow step this prefetch is wasted but harmless: the index check still holds and
+            // the rare branch restarts from the saved cursor and word)
+            nextw = ld_word_if(pw + p, r && p >= first, r ? 0u : nextw);
           } else {
             // rans32 (byte words): up to MAX_RENORM refills, the first from the prefetched word
 #pragma unroll
@@ -525,7 +527,7 @@ __global__ void __maxnreg__(96) pop_bucket_kernel(const __grid_constant__ PopPar
               const bool r = (unsigned long long)x < VT<V>::LB;
               x = r ? (S)((x << VT<V>::WB) | (S)nextw) : x;
               p -= r ? 1 : 0;
-              nextw = ld_word_if(pw + p, r && !slow && p >= first, r ? 0u : nextw);
+              nextw = ld_word_if(pw + p, r && p >= first, r ? 0u : nextw);
             }
             a = addr_of(rown, (uint32_t)x);
           }
