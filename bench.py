@@ -57,6 +57,8 @@ def parse():
     ap.add_argument("--e2e-chunk", type=int, default=4096, help="symbols per column chunk of the host pipeline")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--clocks-dir", default=None,
+                    help="folder that keeps the nvidia-smi samples of the timed region (default: a temporary folder)")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="target CPU work of the baseline sample")
     return ap.parse_args()
 
@@ -95,13 +97,16 @@ class ClockSampler:
          "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
          "clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, gpu_index):
+    def __init__(self, gpu_index, folder=None):
         try:
             self.gpu = "GPU-" + str(torch.cuda.get_device_properties(gpu_index).uuid)
         except Exception:
             self.gpu = str(gpu_index)
         self.proc = None
-        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_rank{gpu_index}.csv")
+        if folder is None:
+            import tempfile
+            folder = tempfile.mkdtemp(prefix="tans_clocks_")
+        self.path = os.path.join(folder, f"clocks_rank{gpu_index}.csv")
 
     def __enter__(self):
         try:
@@ -200,7 +205,7 @@ def run_ours(args, ws, rank, local):
     del dec
     evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clk:
+    with ClockSampler(local, args.clocks_dir) as clk:
         barrier(ws)
         n_launch0 = _C.launch_count()
         t0.record()
@@ -353,7 +358,7 @@ def run_ours_ragged(args, ws, rank, local):
     del dec
     evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clk:
+    with ClockSampler(local, args.clocks_dir) as clk:
         barrier(ws)
         n_launch0 = _C.launch_count()
         t0.record()
