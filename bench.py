@@ -325,7 +325,7 @@ def run_e2e(args, w, ws, rank, dev, _C, push, pop, init_cpu, push_t, pop_t, kw):
 
 # ----------------------------------------------------------------------------- ragged workload
 def run_ours_ragged(args, ws, rank, local):
-    """Configuration 5: streams of different lengths, one cdf row per symbol (ragged ops)."""
+    """ragged_adaptive: streams of different lengths, one cdf row per symbol (ragged ops)."""
     from torch_ans_b200 import _C
     from torch_ans_b200.workloads import ragged_adaptive
     dev = torch.device("cuda", local)

@@ -1,7 +1,7 @@
 """Python face of the oracle: the CPU restatement of torch_ans's rANS path (TEST INFRASTRUCTURE).
 
 Only ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline / reference leg use this
-module, and only as the checker (or as the timed CPU reference); the product package
+module, and only as the oracle the results are compared with (or as the timed CPU reference); the product package
 ``torch_ans_b200`` never imports it.
 
 * The coding loops live in ``oracle/rans_oracle.c`` (plain C, compiled here with gcc into

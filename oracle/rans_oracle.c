@@ -1,7 +1,7 @@
 /*
  * oracle/rans_oracle.c -- CPU restatement of torch_ans's rANS coding path.
  *
- * TEST INFRASTRUCTURE ONLY.  This file is the checker that the CUDA path of torch_ans_b200 is
+ * TEST INFRASTRUCTURE ONLY.  This file is the oracle that the CUDA path of torch_ans_b200 is
  * compared against; nothing in the product imports, links or executes it.  Only tests/,
  * __graft_entry__.smoke() and bench.py's CPU-baseline leg load it (through oracle/oracle.py).
  *
