@@ -1,35 +1,46 @@
 """Benchmark of the rANS coding path: encode + decode Gsymbols/s on 1..8 B200 (one process per GPU).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--workload mixture_invcdf] [--impl ours|reference]
+                    [--scaling strong|weak]
 
 A step is one pass of the coding path over one batch: push (encode) of every stream from a fresh
 stream tensor, then pop (decode) of every stream, through the `_C` op surface, with inputs
-resident in HBM.  ``value`` = symbols of all ranks / max-over-ranks device time of K steps
-(each symbol is encoded once and decoded once per step), in Gsymbols/s.  The default workload
-is the 2^31-symbol rans64 push + inverse-cdf pop configuration (8,192 streams x 262,144
-symbols, 256 tables over 1,024 symbols) per GPU: streams are independent, so N GPUs process N
-such batches (weak scaling) with no collective on the data path.
+resident in HBM.  ``value`` = symbols of the whole job / max-over-ranks device time of K steps
+(each symbol is encoded once and decoded once per step), in Gsymbols/s.  The default workload is
+the 2^31-symbol rans64 push + inverse-cdf pop configuration: 8,192 streams x 262,144 symbols over
+256 tables of 1,024 symbols.
+
+Scaling (``--scaling``):
+  * ``strong`` (default): the configuration's batch is the job; rank r of N codes the contiguous
+    stream range ``shard_streams(8192, N, r)`` (1,024 streams per GPU at N = 8).  With N > 1 the
+    line also carries ``weak_scaling``: every rank coding a whole batch, timed the same way.
+  * ``weak``: every rank codes a whole batch (N batches per job).
 
 Also reported:
-  * ``e2e``: the same round trip through the public API from pinned host memory -- H2D of symbols
-    and indexes, push, device assembly of the concatenated bitstream, D2H of it; H2D of the
-    bitstream and indexes, device parse, pop, D2H of the decoded symbols -- host wall clock, max
-    over ranks.  With N > 1 the ranks all-gather per-stream byte lengths (NCCL) to place their
-    segments in the job-wide bitstream.
+  * ``e2e``: the same round trip through the public host API (``HostStreamCoder``) from pinned
+    host memory: H2D of symbols and indexes overlapped with the push; NCCL all-gather of every
+    stream's byte length (N > 1); device assembly of this rank's records and D2H of them into the
+    job-wide concatenated bitstream at the offsets the lengths give (a host file shared by the
+    ranks, N > 1); then this rank's byte range back in, device parse, pop overlapped with the D2H
+    of the decoded symbols.  Host wall clock, max over ranks.  ``e2e.host_link`` gives the time
+    of plain pinned copies of the same bytes on all ranks at once (the ceiling the e2e can reach).
   * ``roofline``: the dominant kernel's algorithmic bytes (symbol + index + compressed bytes per
     symbol, plus its tables) over its CUDA-event time, against the measured HBM copy bandwidth.
-  * ``cpu_baseline``: the reference CPU implementation (compiled by oracle/build_ref.py) on a
-    bounded sample of the same workload, all host threads.
-``--impl reference`` times only that reference CPU implementation (rank 0), on the same
-workload and metric.
+  * ``cpu_baseline`` (N = 1): the reference CPU implementation (compiled from the reference's
+    sources by oracle/build_ref.py) on a bounded sample of the same workload, all host threads,
+    with the same steps and warm-up as ``--impl reference``.
+  * ``parity``: the GPU's bytes, lengths and decoded symbols against that reference on the same
+    sample (rank 0; at N > 1 a smaller sample).
+``--impl reference`` times only the reference CPU implementation (rank 0), on the same workload
+and metric; that process loads none of this library's native code.
 """
 from __future__ import annotations
 
 import argparse
 import json
-import math
 import os
 import statistics
+import struct
 import subprocess
 import sys
 import time
@@ -51,15 +62,17 @@ def parse():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="mixture_invcdf")
+    ap.add_argument("--scaling", default="strong", choices=["strong", "weak"])
     ap.add_argument("--scale", type=float, default=1.0, help="fraction of the configuration's streams")
     ap.add_argument("--length-scale", type=float, default=1.0, help="fraction of the configuration's stream length")
     ap.add_argument("--e2e-steps", type=int, default=2)
     ap.add_argument("--e2e-chunk", type=int, default=4096, help="symbols per column chunk of the host pipeline")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--parity-streams", type=int, default=64,
+                    help="streams of the byte-parity sample when no CPU-baseline sample is run (N > 1)")
     ap.add_argument("--clocks-dir", default=None,
                     help="folder that keeps the nvidia-smi samples of the timed region (default: a temporary folder)")
-    ap.add_argument("--cpu-seconds", type=float, default=12.0, help="target CPU work of the baseline sample")
     return ap.parse_args()
 
 
@@ -68,9 +81,12 @@ def dist_setup():
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if ws > 1:
-        torch.cuda.set_device(local)
         from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=torch.device("cuda", local))
+        if torch.cuda.is_available():
+            torch.cuda.set_device(local)
+            dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=torch.device("cuda", local))
+        else:
+            dist.init_process_group("gloo", timeout=timedelta(seconds=180))
     elif torch.cuda.is_available():
         torch.cuda.set_device(0)
     return ws, rank, local
@@ -90,6 +106,11 @@ def barrier(ws):
     torch.cuda.synchronize()
 
 
+def reference_steps(steps, warmup):
+    """Seconds of reference CPU work per step, the same for the reference arm and the CPU leg."""
+    return min(10.0, max(2.0, 120.0 / max(1, steps + warmup)))
+
+
 class ClockSampler:
     """nvidia-smi clock/throttle sampling during the timed region."""
 
@@ -97,7 +118,7 @@ class ClockSampler:
          "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
          "clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, gpu_index, folder=None):
+    def __init__(self, gpu_index, folder=None, tag=""):
         try:
             self.gpu = "GPU-" + str(torch.cuda.get_device_properties(gpu_index).uuid)
         except Exception:
@@ -106,7 +127,7 @@ class ClockSampler:
         if folder is None:
             import tempfile
             folder = tempfile.mkdtemp(prefix="tans_clocks_")
-        self.path = os.path.join(folder, f"clocks_rank{gpu_index}.csv")
+        self.path = os.path.join(folder, f"clocks_rank{gpu_index}{tag}.csv")
 
     def __enter__(self):
         try:
@@ -157,34 +178,58 @@ def measured_peak_hbm():
         return 6650.0, "fallback"
 
 
-def build_workload(name, device, scale, length_scale, seed_offset=0):
+def reference_lib():
+    """The compiled reference CPU extension (oracle/_ref), or None."""
+    from oracle import build_ref
+    return build_ref.load()
+
+
+def port_alias_builder():
+    """The oracle's restatement of rans_alias_build_table (for hosts without oracle/_ref)."""
+    from oracle import oracle as O
+
+    def build(cdfs, sizes, symbol_precision=8, freq_precision=16):
+        remap, table, _ = O.alias_build_table(cdfs.numpy(), sizes.numpy(), symbol_precision, freq_precision)
+        return torch.from_numpy(remap), torch.from_numpy(table)
+    return build
+
+
+def build_workload(name, device, scale, length_scale, seed_offset=0, alias_builder=None):
     from torch_ans_b200 import workloads as W
     fn = W.BUILDERS[name]
     kw = dict(device=device, scale=scale)
     if name != "gaussian_latent":
         kw["length_scale"] = length_scale
+    if name == "zipf_alias" and alias_builder is not None:
+        kw["alias_builder"] = alias_builder
     if seed_offset:
         import inspect
         kw["seed"] = inspect.signature(fn).parameters["seed"].default + seed_offset
     return fn(**kw)
 
 
+def shard_of(w, lo, hi):
+    """The workload restricted to streams [lo, hi) (the same object when that is all of them)."""
+    import dataclasses
+    if lo == 0 and hi == w.symbols.shape[0]:
+        return w
+    return dataclasses.replace(w, symbols=w.symbols[lo:hi].contiguous(), indexes=w.indexes[lo:hi].contiguous())
+
+
 # ----------------------------------------------------------------------------- our GPU path
-def run_ours(args, ws, rank, local):
+def time_round_trips(args, w, ws, local, tag=""):
+    """Warm-up, then K timed push + pop steps of the rank's batch `w` (all ranks take part)."""
     from torch_ans_b200 import _C
     dev = torch.device("cuda", local)
-    w = build_workload(args.workload, dev, args.scale, args.length_scale, seed_offset=1000 * rank)
     B, N = w.symbols.shape
-    nsym = B * N
     push = getattr(_C, w.push_op)
     pop = getattr(_C, w.pop_op)
     init = getattr(_C, f"{w.variant}_init_stream")
     kw = dict(freq_precision=w.fp, bypass_coding=w.bypass, bypass_precision=w.bp)
-    init_cpu = init(B)
     push_t, pop_t = w.tables_for_push(), w.tables_for_pop()
 
     def step(ev=None):
-        st = init_cpu.to(dev, non_blocking=True)
+        st = init(B, device=str(dev))  # made on the device: the push resizes without a device read
         if ev:
             ev[0].record()
         push(st, w.symbols, w.indexes, push_t, w.cdfs_sizes, w.offsets, **kw)
@@ -205,7 +250,7 @@ def run_ours(args, ws, rank, local):
     del dec
     evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local, args.clocks_dir) as clk:
+    with ClockSampler(local, args.clocks_dir, tag) as clk:
         barrier(ws)
         n_launch0 = _C.launch_count()
         t0.record()
@@ -214,23 +259,24 @@ def run_ours(args, ws, rank, local):
         t1.record()
         n_launch = _C.launch_count() - n_launch0
         barrier(ws)
-    ok = ok and bool(torch.equal(dec, w.symbols))
+    ok = ok and bool(torch.equal(dec, w.symbols)) and _C.device_status() == 0
     del dec
     ms = t0.elapsed_time(t1) / args.steps
     push_ms = sum(e[0].elapsed_time(e[1]) for e in evs) / args.steps
     pop_ms = sum(e[1].elapsed_time(e[2]) for e in evs) / args.steps
-    ms_max = max_over_ranks(ms, ws)
-    push_ms_max, pop_ms_max = max_over_ranks(push_ms, ws), max_over_ranks(pop_ms, ws)
-    all_ok = max_over_ranks(0.0 if ok else 1.0, ws) == 0.0
-    total = nsym * ws
-    value = total / (ms_max / 1e3) / 1e9
+    return dict(ms=max_over_ranks(ms, ws), push_ms=max_over_ranks(push_ms, ws), pop_ms=max_over_ranks(pop_ms, ws),
+                push_ms_local=push_ms, pop_ms_local=pop_ms, ok=max_over_ranks(0.0 if ok else 1.0, ws) == 0.0,
+                comp_bytes=comp_bytes, n_launch=int(n_launch), clocks=clk.summary(), B=B, N=N)
 
-    # roofline of the dominant kernel (algorithmic bytes / event time)
-    c = comp_bytes / nsym
+
+def roofline(args, w, r, nsym):
+    """Roofline of the dominant kernel on this rank (algorithmic bytes / CUDA-event time)."""
+    push_t, pop_t = w.tables_for_push(), w.tables_for_pop()
+    c = r["comp_bytes"] / nsym
     table_bytes = {"push": push_t.numel() * 4 + 16 * push_t.shape[0], "pop": pop_t.numel() * 4 + 16 * pop_t.shape[0]}
     alg = {"push": nsym * (8 + c) + table_bytes["push"], "pop": nsym * (8 + c) + table_bytes["pop"]}
-    dom = "pop" if pop_ms >= push_ms else "push"
-    dom_ms = pop_ms if dom == "pop" else push_ms
+    dom = "pop" if r["pop_ms_local"] >= r["push_ms_local"] else "push"
+    dom_ms = r["pop_ms_local"] if dom == "pop" else r["push_ms_local"]
     peak, peak_kind = measured_peak_hbm()
     achieved = alg[dom] / (dom_ms / 1e3) / 1e9
     traffic = None
@@ -241,36 +287,103 @@ def run_ours(args, ws, rank, local):
             traffic = ent["dram_bytes_per_symbol"] * nsym
     except Exception:
         pass
-    clocks = clk.summary()
     # the kernels are bound by the latency of one serial step per stream: report it beside the
     # bandwidth roofline (every stream runs its N steps concurrently with the others)
-    step_ns = dom_ms * 1e6 / max(N, 1)
-    step_cycles = step_ns * clocks["sm_mhz"] / 1e3 if clocks.get("sm_mhz") else None
-    res = dict(value=value, ms=ms_max, gpu_launches=int(n_launch), push_ms=push_ms_max, pop_ms=pop_ms_max, ok=all_ok, nsym=nsym, B=B, N=N,
-               comp_bytes_per_symbol=c, clocks=clocks,
-               roofline={"bound": "hbm", "kernel": f"{w.pop_op if dom == 'pop' else w.push_op}",
-                         "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                         "peak_kind": peak_kind, "traffic": traffic,
-                         "algorithmic_bytes_per_launch": alg[dom], "launch_ms": dom_ms,
-                         "serial_step_ns": step_ns, "serial_step_cycles": step_cycles,
-                         "streams_in_flight": B},
-               encode_gsym_s=total / (push_ms_max / 1e3) / 1e9, decode_gsym_s=total / (pop_ms_max / 1e3) / 1e9)
+    step_ns = dom_ms * 1e6 / max(r["N"], 1)
+    mhz = r["clocks"].get("sm_mhz")
+    return {"bound": "hbm", "kernel": f"{w.pop_op if dom == 'pop' else w.push_op}", "achieved": achieved, "peak": peak,
+            "unit": "GB/s", "frac": achieved / peak, "peak_kind": peak_kind, "traffic": traffic,
+            "algorithmic_bytes_per_launch": alg[dom], "launch_ms": dom_ms, "serial_step_ns": step_ns,
+            "serial_step_cycles": step_ns * mhz / 1e3 if mhz else None, "streams_in_flight": r["B"]}
+
+
+def run_ours(args, ws, rank, local):
+    from torch_ans_b200.sharding import shard_streams
+    dev = torch.device("cuda", local)
+    # every rank builds the configuration's whole batch from the same seed: in strong scaling it
+    # codes its shard of it, in weak scaling all of it
+    w_full = build_workload(args.workload, dev, args.scale, args.length_scale)
+    B_cfg, N = w_full.symbols.shape
+    if args.scaling == "strong":
+        shards = [shard_streams(B_cfg, ws, r) for r in range(ws)]
+        lo, hi = shards[rank]
+        w = shard_of(w_full, lo, hi)
+        job_streams = B_cfg
+    else:
+        shards = [(0, B_cfg) for _ in range(ws)]
+        w = w_full
+        job_streams = B_cfg * ws
+    r = time_round_trips(args, w, ws, local)
+    total = job_streams * N
+    res = dict(value=total / (r["ms"] / 1e3) / 1e9, ms=r["ms"], gpu_launches=r["n_launch"], push_ms=r["push_ms"],
+               pop_ms=r["pop_ms"], ok=r["ok"], nsym=total, B=w.symbols.shape[0], N=N, job_streams=job_streams,
+               comp_bytes_per_symbol=r["comp_bytes"] / max(w.symbols.numel(), 1), clocks=r["clocks"],
+               roofline=roofline(args, w, r, w.symbols.numel()),
+               encode_gsym_s=total / (r["push_ms"] / 1e3) / 1e9, decode_gsym_s=total / (r["pop_ms"] / 1e3) / 1e9)
+    if ws > 1 and args.scaling == "strong":
+        # the weak-scaling view: every rank codes the whole batch
+        rw = time_round_trips(args, w_full, ws, local, tag="_weak")
+        tw = B_cfg * N * ws
+        res["weak_scaling"] = {"value": tw / (rw["ms"] / 1e3) / 1e9, "unit": UNIT, "ms_per_step": rw["ms"],
+                               "streams_per_gpu": B_cfg, "push_ms": rw["push_ms"], "pop_ms": rw["pop_ms"],
+                               "bit_exact_roundtrip": rw["ok"], "clocks": rw["clocks"]}
+        res["ok"] = res["ok"] and rw["ok"]
     if not args.no_e2e:
-        res["e2e"] = run_e2e(args, w, ws, rank, dev, _C, push, pop, init_cpu, push_t, pop_t, kw)
-    del w
+        res["e2e"] = run_e2e(args, w, w_full, shards, ws, rank, dev)
+    del w, w_full
     torch.cuda.empty_cache()
     return res
 
 
-def run_e2e(args, w, ws, rank, dev, _C, push, pop, init_cpu, push_t, pop_t, kw):
-    """Round trip through the public host-batch API (torch_ans_b200.host_pipeline.HostStreamCoder):
-    pinned host symbols and indexes in, concatenated bitstream out to pinned host memory, then that
-    bitstream and the indexes back in and the decoded symbols out (host wall clock, max over ranks)."""
+def host_link_ceiling(h2d_bytes, d2h_bytes, ws, dev, reps=2):
+    """Time of plain pinned H2D + D2H copies of the given sizes on every rank at once (one copy
+    per direction on two CUDA streams): the host link's ceiling for the e2e step's traffic."""
+    chunk = 1 << 30
+    nh, nd = max(1, min(h2d_bytes, chunk)), max(1, min(d2h_bytes, chunk))
+    hs = torch.empty(nh, dtype=torch.uint8, pin_memory=True)
+    hd = torch.empty(nd, dtype=torch.uint8, pin_memory=True)
+    ds = torch.empty(nh, dtype=torch.uint8, device=dev)
+    dd = torch.empty(nd, dtype=torch.uint8, device=dev)
+    s1, s2 = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+
+    def once():
+        with torch.cuda.stream(s1):
+            left = h2d_bytes
+            while left > 0:
+                n = min(left, nh)
+                ds[:n].copy_(hs[:n], non_blocking=True)
+                left -= n
+        with torch.cuda.stream(s2):
+            left = d2h_bytes
+            while left > 0:
+                n = min(left, nd)
+                hd[:n].copy_(dd[:n], non_blocking=True)
+                left -= n
+        s1.synchronize()
+        s2.synchronize()
+
+    once()
+    barrier(ws)
+    t = time.perf_counter()
+    for _ in range(reps):
+        once()
+    barrier(ws)
+    el = max_over_ranks((time.perf_counter() - t) / reps, ws)
+    del hs, hd, ds, dd
+    return el
+
+
+def run_e2e(args, w, w_full, shards, ws, rank, dev):
+    """Round trip through the public host-batch API (torch_ans_b200.host_pipeline.HostStreamCoder)
+    from pinned host memory, with the job-wide concatenated bitstream assembled from the per-stream
+    length all-gather (host wall clock, max over ranks)."""
+    from torch_ans_b200 import _C
     from torch_ans_b200.host_pipeline import HostStreamCoder
+    from torch_ans_b200.sharding import JobBitstream, gather_stream_lengths, record_offsets_from_lengths
     B_all, N = w.symbols.shape
     # pinned host buffers per rank: symbols, indexes, decoded symbols (4 B each) and the bitstream;
     # every rank of this host gets an equal share of 40 % of the available host memory, and when
-    # the whole batch does not fit, the round trip runs on its first streams (same workload)
+    # a rank's whole batch does not fit, the round trip runs on its first streams (same workload)
     try:
         import psutil
         avail = psutil.virtual_memory().available
@@ -283,29 +396,58 @@ def run_e2e(args, w, ws, rank, dev, _C, push, pop, init_cpu, push_t, pop_t, kw):
         t = torch.tensor([B], dtype=torch.int64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MIN)
         B = int(t.item())
+    e2e_shards = [(r * B, (r + 1) * B) for r in range(ws)]  # this rank's records in the job bitstream
     h_sym = torch.empty((B, N), dtype=torch.int32, pin_memory=True)
     h_idx = torch.empty((B, N), dtype=torch.int32, pin_memory=True)
     h_out = torch.empty((B, N), dtype=torch.int32, pin_memory=True)
     h_sym.copy_(w.symbols[:B])
     h_idx.copy_(w.indexes[:B])
     torch.cuda.synchronize()
-    coder = HostStreamCoder(w.variant, push_t, pop_t, w.cdfs_sizes, w.offsets, freq_precision=w.fp,
-                            bypass_coding=w.bypass, bypass_precision=w.bp, alias=w.push_cdfs is not None,
-                            lookup=w.lookup, device=dev, chunk_symbols=args.e2e_chunk)
+    coder = HostStreamCoder(w.variant, w.tables_for_push(), w.tables_for_pop(), w.cdfs_sizes, w.offsets,
+                            freq_precision=w.fp, bypass_coding=w.bypass, bypass_precision=w.bp,
+                            alias=w.push_cdfs is not None, lookup=w.lookup, device=dev, chunk_symbols=args.e2e_chunk)
+    job = None
+    h_in = None
     h2d = d2h = 0
+    state = {}
 
     def once():
-        nonlocal h2d, d2h
-        packed = coder.encode(h_sym, h_idx)
-        if ws > 1:  # place this rank's records in the job-wide bitstream (sizes all-gather, NCCL)
-            from torch_ans_b200.sharding import record_offsets
-            record_offsets(packed.numel(), device=dev)
-        coder.decode(packed, h_idx, out=h_out)
-        h2d = 2 * B * N * 4 + B * N * 4 + packed.numel()
-        d2h = packed.numel() + B * N * 4
-        return packed.numel()
+        nonlocal job, h_in, h2d, d2h
+        stream = coder.encode_to_device(h_sym, h_idx)
+        if ws > 1:
+            lens = gather_stream_lengths(stream[:, 0].contiguous(), e2e_shards)  # NCCL, one int32 per stream
+            offs, total = record_offsets_from_lengths(lens)
+            lo, hi = e2e_shards[rank]
+            start = int(offs[lo])
+            end = int(offs[hi]) if hi < len(lens) else total
+            if job is None:  # first round: rank 0 makes the job file with the job's total size
+                name = [JobBitstream.default_path(f"{os.getpid()}", total) if rank == 0 else None]
+                dist.broadcast_object_list(name, src=0)
+                job = JobBitstream(name[0])
+                if rank == 0:
+                    job.create(total)
+                dist.barrier()
+                job.open()
+                state.update(total=total, lens=lens, offs=offs)
+            elif total != state["total"]:
+                raise RuntimeError("job bitstream size changed between identical steps")
+            local = coder.container_to_host(stream)
+            del stream
+            if local.numel() != end - start:
+                raise RuntimeError("this rank's records do not match the gathered lengths")
+            job.write(start, local)
+            if h_in is None or h_in.numel() < local.numel():
+                h_in = torch.empty(local.numel(), dtype=torch.uint8, pin_memory=True)
+            data = job.read(start, h_in[: end - start])
+        else:
+            data = coder.container_to_host(stream)
+            del stream
+        coder.decode(data, h_idx, out=h_out)
+        h2d = 2 * B * N * 4 + B * N * 4 + data.numel()
+        d2h = data.numel() + B * N * 4
+        return data.numel()
 
-    once()  # warm-up (pinned buffer allocation, table prep)
+    once()  # warm-up (pinned buffer allocation, table prep, job file)
     ok = bool(torch.equal(h_out, h_sym))
     barrier(ws)
     t = time.perf_counter()
@@ -315,12 +457,44 @@ def run_e2e(args, w, ws, rank, dev, _C, push, pop, init_cpu, push_t, pop_t, kw):
     el = (time.perf_counter() - t) / args.e2e_steps
     ok = ok and bool(torch.equal(h_out, h_sym)) and coder.device_status() == 0
     el = max_over_ranks(el, ws)
-    all_ok = max_over_ranks(0.0 if ok else 1.0, ws) == 0.0
-    del h_sym, h_idx, h_out, coder
-    return {"value": B * N * ws / el / 1e9, "unit": UNIT, "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
-            "ms_per_step": el * 1e3, "ok": all_ok, "streams_per_gpu": B, "of_streams_per_gpu": B_all,
-            "path": "pinned host -> HostStreamCoder.encode (column chunks: H2D || push) -> bitstream on host -> "
-                    "HostStreamCoder.decode (H2D || pop || D2H) -> pinned host"}
+    res = {"value": B * N * ws / el / 1e9, "unit": UNIT, "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
+           "ms_per_step": el * 1e3, "streams_per_gpu": B, "of_streams_per_gpu": B_all}
+    if ws > 1:
+        # the job bitstream against single-process records: rank 0 pushes the first and the last
+        # stream of every rank's range on its own and compares their records byte for byte
+        checked = 0
+        if rank == 0:
+            lens, offs = state["lens"], state["offs"]
+            pick = sorted({(r, j) for r in range(ws) for j in (0, B - 1)})
+            rows = [shards[r][0] + j for r, j in pick]  # stream of the configuration each record codes
+            ws_ = w_full.symbols[rows].contiguous()
+            wi_ = w_full.indexes[rows].contiguous()
+            st = getattr(_C, f"{w.variant}_init_stream")(len(rows), device=str(dev))
+            getattr(_C, w.push_op)(st, ws_, wi_, w.tables_for_push(), w.cdfs_sizes, w.offsets, freq_precision=w.fp,
+                                   bypass_coding=w.bypass, bypass_precision=w.bp)
+            alone = _C.rans_stream_to_byte_strings(st)
+            for (r, j), rec in zip(pick, alone):
+                g = e2e_shards[r][0] + j
+                got = job.read(int(offs[g]), torch.empty(4 + len(rec), dtype=torch.uint8)).numpy().tobytes()
+                ok = ok and got == struct.pack("<I", len(rec)) + rec and int(lens[g]) == len(rec)
+                checked += 1
+        dist.barrier()
+        job.close(unlink=(rank == 0))
+        res["job_bitstream"] = {"bytes": int(state["total"]), "records": int(B * ws), "records_checked": checked,
+                                "against": "records of the same streams pushed alone on one GPU",
+                                "collective": "all_gather of one int32 length per stream (NCCL)"}
+    res["ok"] = max_over_ranks(0.0 if ok else 1.0, ws) == 0.0
+    del h_sym, h_idx, h_out, coder, h_in
+    ceil_s = host_link_ceiling(int(h2d), int(d2h), ws, dev)
+    res["host_link"] = {"copy_only_ms": ceil_s * 1e3, "h2d_gbs": h2d * ws / ceil_s / 1e9 if ceil_s else None,
+                        "d2h_gbs": d2h * ws / ceil_s / 1e9 if ceil_s else None,
+                        "e2e_frac_of_copy_ceiling": ceil_s / el if el else None,
+                        "how": "plain pinned H2D and D2H copies of the step's bytes, both directions at once, "
+                               "all ranks at once, max over ranks"}
+    res["path"] = ("pinned host -> HostStreamCoder.encode_to_device (column chunks: H2D || push) -> per-stream length "
+                   "all-gather -> device assembly of this rank's records -> D2H into the job bitstream at the scanned "
+                   "offset -> this rank's byte range -> HostStreamCoder.decode (H2D || pop || D2H) -> pinned host")
+    return res
 
 
 # ----------------------------------------------------------------------------- ragged workload
@@ -334,11 +508,11 @@ def run_ours_ragged(args, ws, rank, local):
     push = getattr(_C, f"{w.variant}_push_ragged")
     pop = getattr(_C, f"{w.variant}_pop_ragged")
     kw = dict(freq_precision=w.fp, bypass_coding=w.bypass, bypass_precision=w.bp)
-    init_cpu = getattr(_C, f"{w.variant}_init_stream")(B)
+    init = getattr(_C, f"{w.variant}_init_stream")
     lengths = (w.row_starts[1:] - w.row_starts[:-1]).cpu()
 
     def step(ev=None):
-        st = init_cpu.to(dev, non_blocking=True)
+        st = init(B, device=str(dev))
         if ev:
             ev[0].record()
         push(st, w.symbols, w.row_starts, w.cdfs, w.cdfs_sizes, offsets=w.offsets, **kw)
@@ -387,8 +561,8 @@ def run_ours_ragged(args, ws, rank, local):
     peak, peak_kind = measured_peak_hbm()
     achieved = alg[dom] / (dom_ms / 1e3) / 1e9
     res = dict(value=total / (ms_max / 1e3) / 1e9, ms=ms_max, gpu_launches=int(n_launch), push_ms=push_ms_max,
-               pop_ms=pop_ms_max, ok=all_ok, nsym=T, B=B, N=int(lengths.max()), comp_bytes_per_symbol=c,
-               clocks=clk.summary(),
+               pop_ms=pop_ms_max, ok=all_ok, nsym=T, B=B, N=int(lengths.max()), job_streams=B * ws,
+               comp_bytes_per_symbol=c, clocks=clk.summary(),
                roofline={"bound": "hbm", "kernel": f"{w.variant}_{dom}_ragged", "achieved": achieved, "peak": peak,
                          "unit": "GB/s", "frac": achieved / peak, "peak_kind": peak_kind, "traffic": None,
                          "algorithmic_bytes_per_launch": alg[dom], "launch_ms": dom_ms},
@@ -405,8 +579,7 @@ _RAGGED_REF = None
 def _ragged_ref_init():
     global _RAGGED_REF
     torch.set_num_threads(1)
-    from oracle import build_ref
-    _RAGGED_REF = build_ref.load()
+    _RAGGED_REF = reference_lib()
 
 
 def _ragged_ref_worker(task):
@@ -444,9 +617,8 @@ def cpu_reference_ragged(seconds, scale, length_scale):
     separate processes (the reference op on B = 1 runs on one thread), timed as the slowest
     worker's push + pop loop."""
     import multiprocessing as mp
-    from oracle import build_ref
     from torch_ans_b200.workloads import ragged_lengths
-    if build_ref.load() is None:
+    if reference_lib() is None:
         return None
     threads = len(os.sched_getaffinity(0))
     lengths = ragged_lengths(max(1, int(4096 * scale)), length_scale, 4).tolist()
@@ -478,22 +650,28 @@ def cpu_reference_ragged(seconds, scale, length_scale):
 
 
 # ----------------------------------------------------------------------------- reference CPU
-def cpu_reference(workload_name, seconds, scale, length_scale, steps=1, warmup=0):
+def cpu_reference(workload_name, seconds, scale, length_scale, steps=1, warmup=0, keep_sample=False,
+                  max_streams=None):
     """Time the reference CPU implementation (oracle/_ref, else the oracle's C port) on a
     bounded sample of the workload: S streams of the configuration (same tables, same stream
-    length), S chosen so one push + pop takes about `seconds` on all host threads."""
-    from oracle import build_ref
-    ref = build_ref.load()
+    length), S chosen so one push + pop takes about `seconds` on all host threads.  Every table,
+    alias tables included, is made by the reference's own code.  With `keep_sample` the sample and
+    the reference's pushed stream come back too (for the byte-parity check)."""
+    ref = reference_lib()
     kind = "reference" if ref is not None else "port"
+    alias_builder = ref.rans_alias_build_table if ref is not None else port_alias_builder()
     threads = len(os.sched_getaffinity(0))
     torch.set_num_threads(threads)
     # the stream count of the full configuration, from a probe with one-symbol streams
-    probe = build_workload(workload_name, "cpu", scale=scale, length_scale=1e-9)
+    probe = build_workload(workload_name, "cpu", scale=scale, length_scale=1e-9, alias_builder=alias_builder)
     b_full = probe.symbols.shape[0]
     del probe
 
     def make(nstreams):
-        return build_workload(workload_name, "cpu", scale=scale * nstreams / b_full, length_scale=length_scale)
+        return build_workload(workload_name, "cpu", scale=scale * nstreams / b_full, length_scale=length_scale,
+                              alias_builder=alias_builder)
+
+    pushed = {}
 
     def run(w):
         B = w.symbols.shape[0]
@@ -504,6 +682,8 @@ def cpu_reference(workload_name, seconds, scale, length_scale, steps=1, warmup=0
             t0 = time.perf_counter()
             getattr(ref, w.push_op)(st, w.symbols, w.indexes, push_t, w.cdfs_sizes, w.offsets, **kw)
             t1 = time.perf_counter()
+            if keep_sample:
+                pushed["stream"] = st.clone()
             dec = getattr(ref, w.pop_op)(st, w.indexes, pop_t, w.cdfs_sizes, w.offsets, **kw)
             t2 = time.perf_counter()
         else:
@@ -513,6 +693,8 @@ def cpu_reference(workload_name, seconds, scale, length_scale, steps=1, warmup=0
             st, _ = O.push(w.variant, st, w.symbols.numpy(), w.indexes.numpy(), push_t.numpy(), w.cdfs_sizes.numpy(),
                            w.offsets.numpy(), w.fp, w.bypass, w.bp, alias=w.lookup == "alias", threads=threads)
             t1 = time.perf_counter()
+            if keep_sample:
+                pushed["stream"] = torch.from_numpy(st.copy())
             dec, _ = O.pop(w.variant, st, w.indexes.numpy(), pop_t.numpy(), w.cdfs_sizes.numpy(), w.offsets.numpy(),
                            w.fp, w.bypass, w.bp, lookup=w.lookup, threads=threads)
             dec = torch.from_numpy(dec)
@@ -521,6 +703,8 @@ def cpu_reference(workload_name, seconds, scale, length_scale, steps=1, warmup=0
         return t1 - t0, t2 - t1
 
     n = min(b_full, max(threads, 1))
+    if max_streams is not None:
+        n = min(b_full, max_streams) if seconds <= 0 else min(n, max_streams)
     w = make(n)
     tp, tq = run(w)
     per_stream = (tp + tq) / n
@@ -529,6 +713,8 @@ def cpu_reference(workload_name, seconds, scale, length_scale, steps=1, warmup=0
     # the whole reference run stay within a few minutes on any host
     N_full = w.symbols.shape[1]
     n2 = max(n, min(n2, (1 << 28) // max(N_full, 1)))
+    if max_streams is not None:
+        n2 = min(n2, max_streams)
     if n2 >= threads:
         n2 = n2 // threads * threads
     if n2 > n:
@@ -545,62 +731,108 @@ def cpu_reference(workload_name, seconds, scale, length_scale, steps=1, warmup=0
     tp, tq = sum(tps) / len(tps), sum(tqs) / len(tqs)
     N = w.symbols.shape[1]
     nsym = n * N
-    return {"value": nsym / (tp + tq) / 1e9, "unit": UNIT, "cores": threads, "kind": kind,
-            "sample": f"{n} of {b_full} streams x {N} symbols ({nsym} symbols) of {workload_name}, push + pop",
-            "encode_gsym_s": nsym / tp / 1e9, "decode_gsym_s": nsym / tq / 1e9, "ms_per_step": (tp + tq) * 1e3}
+    out = {"value": nsym / (tp + tq) / 1e9, "unit": UNIT, "cores": threads, "kind": kind,
+           "sample": f"{n} of {b_full} streams x {N} symbols ({nsym} symbols) of {workload_name}, push + pop, "
+                     f"{max(1, steps)} timed step(s) after {warmup} warm-up",
+           "encode_gsym_s": nsym / tp / 1e9, "decode_gsym_s": nsym / tq / 1e9, "ms_per_step": (tp + tq) * 1e3}
+    if keep_sample:
+        return out, w, pushed["stream"]
+    return out
+
+
+def check_parity(w, ref_stream, kind, dev):
+    """Push and pop the reference's sample on the GPU through `_C` and compare row lengths,
+    payload bytes and decoded symbols with the reference's."""
+    from torch_ans_b200 import _C
+    B = w.symbols.shape[0]
+    kw = dict(freq_precision=w.fp, bypass_coding=w.bypass, bypass_precision=w.bp)
+    sym, idx = w.symbols.to(dev), w.indexes.to(dev)
+    st = getattr(_C, f"{w.variant}_init_stream")(B, device=str(dev))
+    getattr(_C, w.push_op)(st, sym, idx, w.tables_for_push().to(dev), w.cdfs_sizes.to(dev), w.offsets.to(dev), **kw)
+    lens_equal = bool(torch.equal(st[:, 0].cpu(), ref_stream[:, 0]))
+    ours = _C.rans_stream_to_byte_strings(st)
+    theirs = [ref_stream[b, 1:].numpy().tobytes()[: int(ref_stream[b, 0])] for b in range(B)]
+    bytes_equal = lens_equal and ours == theirs
+    width_equal = st.shape[1] == ref_stream.shape[1]
+    dec = getattr(_C, w.pop_op)(st, idx, w.tables_for_pop().to(dev), w.cdfs_sizes.to(dev), w.offsets.to(dev), **kw)
+    decode_equal = bool(torch.equal(dec.cpu(), w.symbols))
+    status = _C.device_status()
+    del st, dec, sym, idx
+    return {"streams_checked": B, "symbols_checked": int(w.symbols.numel()), "bytes_equal": bytes_equal,
+            "lengths_equal": lens_equal, "row_width_equal": width_equal, "decode_equal": decode_equal,
+            "device_status": status, "against": "oracle/_ref (the reference CPU path)" if kind == "reference"
+            else "the oracle's C port"}
+
+
+def reference_arm(args, ws, rank, cfg):
+    """--impl reference: the reference's own CPU implementation only (rank 0)."""
+    if rank == 0:
+        per_step = reference_steps(args.steps, args.warmup)
+        if args.workload == "ragged_adaptive":
+            base = cpu_reference_ragged(per_step * 4, args.scale, args.length_scale)
+        else:
+            base = cpu_reference(args.workload, per_step, args.scale, args.length_scale, steps=args.steps,
+                                 warmup=args.warmup)
+        if base is None:
+            print(json.dumps({"impl": "reference", "unavailable": "the reference CPU library (oracle/_ref) is "
+                              "not built on this machine"}), flush=True)
+        else:
+            line = {"metric": METRIC, "value": base["value"], "unit": UNIT, "n_gpus": ws, "steps": args.steps,
+                    "warmup": args.warmup, "ms_per_step": base["ms_per_step"], "higher_is_better": True,
+                    "scaling": args.scaling, "vs_baseline": None, "dtype": "int64", "data": "synthetic", "config": cfg,
+                    "impl": "reference", "cpu_baseline": base,
+                    "e2e": {"value": base["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+            print(json.dumps(line), flush=True)
 
 
 def main():
     args = parse()
     ws, rank, local = dist_setup()
-    cfg = {"workload": args.workload, "scale": args.scale, "length_scale": args.length_scale,
-           "l2": "inputs larger than L2 (no flush)", "parallelism": f"stream shards x{ws}" if ws > 1 else "single GPU"}
     ragged = args.workload == "ragged_adaptive"
+    cfg = {"workload": args.workload, "scale": args.scale, "length_scale": args.length_scale,
+           "l2": "inputs larger than L2 (no flush)",
+           "parallelism": (f"stream shards x{ws} ({args.scaling} scaling)" if ws > 1 else "single GPU")}
     if args.impl == "reference":
-        if rank == 0:
-            per_step = min(10.0, max(2.0, 120.0 / max(1, args.steps + args.warmup)))
-            if ragged:
-                base = cpu_reference_ragged(per_step * 4, args.scale, args.length_scale)
-            else:
-                base = cpu_reference(args.workload, per_step, args.scale, args.length_scale, steps=args.steps,
-                                     warmup=args.warmup)
-            if base is None:
-                print(json.dumps({"impl": "reference", "unavailable": "the reference CPU library (oracle/_ref) is "
-                                  "not built on this machine"}), flush=True)
-                if ws > 1:
-                    dist.destroy_process_group()
-                return
-            line = {"metric": METRIC, "value": base["value"], "unit": UNIT, "n_gpus": ws, "steps": args.steps,
-                    "warmup": args.warmup, "ms_per_step": base["ms_per_step"], "higher_is_better": True, "scaling": "weak",
-                    "vs_baseline": None, "dtype": "int64", "data": "synthetic", "config": cfg, "impl": "reference",
-                    "cpu_baseline": base,
-                    "e2e": {"value": base["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-            print(json.dumps(line), flush=True)
+        reference_arm(args, ws, rank, cfg)
         if ws > 1:
             dist.destroy_process_group()
         return
 
+    if ragged and args.scaling == "strong" and ws > 1:
+        args.scaling = "weak"  # the ragged workload runs one batch per rank
     res = run_ours_ragged(args, ws, rank, local) if ragged else run_ours(args, ws, rank, local)
-    base = None
-    if rank == 0 and ws == 1 and not args.no_cpu:
-        if ragged:
-            base = cpu_reference_ragged(args.cpu_seconds, args.scale, args.length_scale)
+    base = parity = None
+    dev = torch.device("cuda", local)
+    if rank == 0 and not ragged:
+        per_step = reference_steps(args.steps, args.warmup)
+        if ws == 1 and not args.no_cpu:
+            base, sample, ref_stream = cpu_reference(args.workload, per_step, args.scale, args.length_scale,
+                                                     steps=args.steps, warmup=args.warmup, keep_sample=True)
         else:
-            base = cpu_reference(args.workload, args.cpu_seconds, args.scale, args.length_scale)
+            _, sample, ref_stream = cpu_reference(args.workload, 0.0, args.scale, args.length_scale, steps=1,
+                                                  warmup=0, keep_sample=True, max_streams=args.parity_streams)
+        parity = check_parity(sample, ref_stream, (base or {"kind": "reference" if reference_lib() else "port"})["kind"],
+                              dev)
+        del sample, ref_stream
+    elif rank == 0 and ws == 1 and not args.no_cpu:
+        base = cpu_reference_ragged(reference_steps(args.steps, args.warmup) * 4, args.scale, args.length_scale)
+    if ws > 1:
+        dist.barrier()
     if rank == 0:
         if "lengths" in res:
             cfg["ragged_lengths"] = res["lengths"]
-        cfg.update({"streams_per_gpu": res["B"], "symbols_per_stream": res["N"], "global_batch_streams": res["B"] * ws,
+        cfg.update({"streams_per_gpu": res["B"], "symbols_per_stream": res["N"], "global_batch_streams": res["job_streams"],
                     "compressed_bytes_per_symbol": round(res["comp_bytes_per_symbol"], 4)})
         line = {"metric": METRIC, "value": res["value"], "unit": UNIT, "n_gpus": ws, "steps": args.steps,
-                "warmup": args.warmup, "ms_per_step": res["ms"], "higher_is_better": True, "scaling": "weak",
+                "warmup": args.warmup, "ms_per_step": res["ms"], "higher_is_better": True, "scaling": args.scaling,
                 "vs_baseline": None, "dtype": "int64", "data": "synthetic", "config": cfg,
                 "encode_gsym_s": res["encode_gsym_s"], "decode_gsym_s": res["decode_gsym_s"],
                 "push_ms": res["push_ms"], "pop_ms": res["pop_ms"], "bit_exact_roundtrip": res["ok"],
                 "roofline": res["roofline"], "clocks": res["clocks"],
-                "gpu_launches": res["gpu_launches"], "cpu_baseline": base}
-        if "e2e" in res:
-            line["e2e"] = res["e2e"]
+                "gpu_launches": res["gpu_launches"], "cpu_baseline": base, "parity": parity}
+        for k in ("e2e", "weak_scaling"):
+            if k in res:
+                line[k] = res[k]
         print(json.dumps(line), flush=True)
     if ws > 1:
         dist.barrier()

@@ -2,9 +2,10 @@
 
 The reference's own CPU backend (``torch_ans/rans_cpu.cpp`` + ``torch_ans/rans_utils.hpp``),
 its dispatch/serialisation glue (``torch_ans/rans.cpp``, ``torch_ans/rans.hpp``) and its pybind
-module (``torch_ans/lib.cpp``) are compiled with g++ straight from the files where they lie under
-``/root/reference`` -- the reference's setup.py is not run and no source is copied into this
-repository.  The result is ``oracle/_ref/torch_ans_ref/_C<ext>.so`` (git-ignored; it travels to the
+module (``torch_ans/lib.cpp``) are compiled with g++ straight from the files where they lie in the
+reference checkout -- the reference's setup.py is not run and no source is copied into this
+repository.  The checkout is the folder named by the ``TORCH_ANS_REFERENCE`` environment variable,
+else a folder ``reference`` beside this repository's root.  The result is ``oracle/_ref/torch_ans_ref/_C<ext>.so`` (git-ignored; it travels to the
 GPU box next to the library's own built files).  It exposes exactly the reference ``_C`` surface
 (``rans64_push`` ...) on CPU tensors and is used by:
 
@@ -16,7 +17,7 @@ Build flags follow the reference build (``setup.py:33-40``: ``-std=c++17 -O3 -fo
 ``-march=native``, replaced by ``-march=x86-64-v3`` so the binary built here also runs on the GPU
 box's host CPU.  ``WITH_CUDA`` is not defined, so only the CPU path is built.
 
-Usage: ``python oracle/build_ref.py [--reference /root/reference] [--force]``
+Usage: ``python oracle/build_ref.py [--reference PATH] [--force]``
 """
 from __future__ import annotations
 
@@ -31,12 +32,21 @@ OUT_DIR = os.path.join(HERE, "_ref", "torch_ans_ref")
 SOURCES = ("torch_ans/lib.cpp", "torch_ans/rans.cpp", "torch_ans/rans_cpu.cpp")
 
 
+def default_reference() -> str:
+    """The reference checkout: $TORCH_ANS_REFERENCE, else ``reference`` beside the repository."""
+    env = os.environ.get("TORCH_ANS_REFERENCE")
+    if env:
+        return env
+    return os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference")
+
+
 def target_path() -> str:
     return os.path.join(OUT_DIR, "_C" + sysconfig.get_config_var("EXT_SUFFIX"))
 
 
-def build(reference: str = "/root/reference", force: bool = False, verbose: bool = True) -> str | None:
+def build(reference: str | None = None, force: bool = False, verbose: bool = True) -> str | None:
     """Compile the reference CPU extension; returns the .so path, or None when the sources are absent."""
+    reference = reference or default_reference()
     out = target_path()
     srcs = [os.path.join(reference, s) for s in SOURCES]
     if not all(os.path.exists(s) for s in srcs):
@@ -92,7 +102,7 @@ def load():
 
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=None, help="reference checkout (default: $TORCH_ANS_REFERENCE or ../reference)")
     ap.add_argument("--force", action="store_true")
     a = ap.parse_args()
     r = build(a.reference, a.force)

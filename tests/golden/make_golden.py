@@ -14,7 +14,8 @@ bypass-off Laplace-like tables, inverse-cdf rows, alias tables, the 4-way interl
 pushes onto non-empty streams with partial pops, and edge shapes (1 symbol, odd lengths,
 single-symbol alphabets, large escape values).
 
-Run (in the build container, where /root/reference exists):
+Run where the reference checkout exists ($TORCH_ANS_REFERENCE, or ``reference`` beside this
+repository):
     python oracle/build_ref.py && python tests/golden/make_golden.py
 """
 from __future__ import annotations

@@ -16,6 +16,7 @@
 #include <cstdlib>
 #include <tuple>
 #include <mutex>
+#include <unordered_map>
 #include <optional>
 #include <string>
 #include <vector>
@@ -87,11 +88,78 @@ Tensor on_device_i32(const Tensor& t, const at::Device& dev, const char* name) {
 
 void* cur_stream() { return (void*)at::cuda::getCurrentCUDAStream().stream(); }
 
-// rans_init_stream (torch_ans/rans_cpu.cpp:22-41): a CPU tensor, as in the reference
+// ------------------------------------------------------------------ stream lengths the host knows
+// The worst-case resize before a push (rans.hpp:105-124) needs the largest row length of the
+// stream.  On a CUDA stream that is device data, and reading it blocks the host until the GPU
+// has finished all work queued before it.  A stream this module has just made on a device
+// (rans*_init_stream(..., device=...)) has every length equal to num_interleaves x state bytes,
+// so its largest length is recorded here and the next push resizes without reading the device.
+// An entry is tied to the tensor's storage (a weak reference, so a freed and reused address never
+// matches), its view and its version counter (any in-place change through torch invalidates it);
+// every coding op drops the entry of the stream it changes.  Inference tensors carry no version
+// counter and are never recorded.
+struct KnownLength {
+  c10::weak_intrusive_ptr<c10::StorageImpl> storage;
+  uint32_t version = 0;
+  int64_t storage_offset = 0, rows = 0, width = 0;
+  int64_t max_len = 0;
+};
+std::mutex g_known_mu;
+std::unordered_map<const void*, KnownLength> g_known;
+
+void remember_length(const Tensor& s, int64_t max_len) {
+  if (s.is_inference()) return;
+  KnownLength k{c10::weak_intrusive_ptr<c10::StorageImpl>(s.storage().getWeakStorageImpl()),
+                s.unsafeGetTensorImpl()->version_counter().current_version(), s.storage_offset(), s.size(0), s.size(1),
+                max_len};
+  std::lock_guard<std::mutex> g(g_known_mu);
+  if (g_known.size() > 4096) {  // drop entries whose storage is gone
+    for (auto it = g_known.begin(); it != g_known.end();) it = it->second.storage.expired() ? g_known.erase(it) : ++it;
+  }
+  g_known.insert_or_assign(s.storage().unsafeGetStorageImpl(), std::move(k));
+}
+
+void forget_length(const Tensor& s) {
+  std::lock_guard<std::mutex> g(g_known_mu);
+  g_known.erase(s.storage().unsafeGetStorageImpl());
+}
+
+std::optional<int64_t> known_length(const Tensor& s) {
+  if (s.is_inference()) return std::nullopt;
+  std::lock_guard<std::mutex> g(g_known_mu);
+  auto it = g_known.find(s.storage().unsafeGetStorageImpl());
+  if (it == g_known.end()) return std::nullopt;
+  const KnownLength& k = it->second;
+  auto alive = k.storage.lock();
+  if (!alive || alive.get() != s.storage().unsafeGetStorageImpl() ||
+      k.version != s.unsafeGetTensorImpl()->version_counter().current_version() ||
+      k.storage_offset != s.storage_offset() || k.rows != s.size(0) || k.width != s.size(1)) {
+    g_known.erase(it);
+    return std::nullopt;
+  }
+  return k.max_len;
+}
+
+// rans_init_stream (torch_ans/rans_cpu.cpp:22-41): a CPU tensor, as in the reference.  With a
+// CUDA `device` (an addition) the same rows are made on that device by a kernel, with no host
+// copy, and the stream's lengths are recorded so that the first push needs no device read.
 template <int V>
-Tensor init_stream(int64_t size, int64_t num_interleaves, int64_t preallocate_size) {
+Tensor init_stream(int64_t size, int64_t num_interleaves, int64_t preallocate_size, std::optional<std::string> device) {
   const int sb = kStateBytes[V];
   const int64_t width = 1 + preallocate_size / 4 + num_interleaves * ((sb + 3) / 4);
+  if (device.has_value()) {
+    at::Device dev(*device);
+    TORCH_CHECK(dev.is_cuda(), "torch_ans_b200: init_stream(device=...) makes CUDA streams only");
+    if (!dev.has_index()) dev = at::Device(at::kCUDA, c10::cuda::current_device());
+    TORCH_CHECK(num_interleaves >= 1, "torch_ans_b200: num_interleaves must be >= 1");
+    c10::cuda::CUDAGuard guard(dev);
+    Tensor s = torch::empty({size, width}, torch::TensorOptions().dtype(torch::kInt32).device(dev));
+    if (size > 0)
+      check_rc(tans_init_stream(V, (int)num_interleaves, s.data_ptr<int32_t>(), size, width, cur_stream()),
+               "init_stream");
+    if (size > 0) remember_length(s, sb * num_interleaves);
+    return s;
+  }
   Tensor s = torch::zeros({size, width}, torch::TensorOptions().dtype(torch::kInt32));
   int32_t* p = s.data_ptr<int32_t>();
   const uint64_t lb = 1ull << (8 * sb - 1 - (V == 0 ? 32 : (V == 1 ? 8 : 16)));
@@ -107,10 +175,17 @@ Tensor init_stream(int64_t size, int64_t num_interleaves, int64_t preallocate_si
 void resize_for_push(Tensor& stream, int64_t num_symbols, int64_t freq_precision, bool bypass) {
   const int64_t B = stream.size(0), W = stream.size(1);
   if (B == 0) return;
-  Tensor mx = torch::empty({1}, stream.options());
-  check_rc(tans_stream_max_length(stream.data_ptr<int32_t>(), B, W, mx.data_ptr<int32_t>(), cur_stream()),
-           "stream length reduction");
-  const int64_t max_len = mx.item<int32_t>();
+  int64_t max_len;
+  if (auto k = known_length(stream)) {
+    max_len = *k;  // a stream made on the device by init_stream: no device read
+  } else {
+    // the reference reads the maximum back too (rans.hpp:106, `.item()`): the new width depends on it
+    Tensor mx = torch::empty({1}, stream.options());
+    check_rc(tans_stream_max_length(stream.data_ptr<int32_t>(), B, W, mx.data_ptr<int32_t>(), cur_stream()),
+             "stream length reduction");
+    max_len = mx.item<int32_t>();
+  }
+  forget_length(stream);  // the push about to run changes the lengths
   int64_t safe = max_len + (num_symbols * freq_precision + 7) / 8;
   if (bypass) safe += num_symbols * (int64_t)sizeof(int32_t);
   if (safe < max_len) throw py::value_error("Overflow!");
@@ -176,6 +251,7 @@ Tensor rans_pop(Tensor stream, std::optional<Tensor> indexes, std::optional<Tens
   TORCH_CHECK(cdfs_sizes.has_value());
   const at::Device dev = stream.device();
   c10::cuda::CUDAGuard guard(dev);
+  forget_length(stream);
   Tensor idx = on_device_i32(*indexes, dev, "indexes");
   TORCH_CHECK(idx.dim() == 2 && idx.size(0) == stream.size(0),
               "torch_ans_b200: indexes must be (batch, symbols) with one row per stream row");
@@ -255,6 +331,7 @@ void rans_push_ragged(Tensor stream, Tensor symbols, Tensor row_starts, Tensor c
     off = on_device_i32(*offsets, dev, "offsets");
     TORCH_CHECK(off.size(0) == cdf.size(0), "torch_ans_b200: offsets must have one entry per cdf row");
   }
+  forget_length(stream);
   resize_for_ragged_push(stream, rows, freq_precision, bypass_coding);
   Tensor ws = torch::empty({(int64_t)tans_push_ragged_workspace_size(T) + 256},
                            torch::TensorOptions().dtype(torch::kUInt8).device(dev));
@@ -294,6 +371,7 @@ Tensor rans_pop_ragged(Tensor stream, Tensor row_starts, Tensor cdfs, Tensor cdf
     off = on_device_i32(*offsets, dev, "offsets");
     TORCH_CHECK(off.size(0) == cdf.size(0), "torch_ans_b200: offsets must have one entry per cdf row");
   }
+  forget_length(stream);
   Tensor out = torch::zeros({T}, torch::TensorOptions().dtype(torch::kInt32).device(dev));
   Tensor& st = status_word(dev);
   const int rc = tans_pop_ragged(V, stream.data_ptr<int32_t>(), B, stream.size(1), out.data_ptr<int32_t>(),
@@ -713,7 +791,8 @@ int64_t device_status(std::optional<int64_t> device, bool reset) {
   py::arg("stream"), py::arg("indexes") = py::none(), py::arg("cdfs") = py::none(),                       \
       py::arg("cdfs_sizes") = py::none(), py::arg("offsets") = py::none(), py::arg("symbol_precision") = 8, \
       py::arg("freq_precision") = 16, py::arg("bypass_coding") = true, py::arg("bypass_precision") = 4
-#define TANS_INIT_ARGS py::arg("size"), py::arg("num_interleaves") = 1, py::arg("preallocate_size") = 0
+#define TANS_INIT_ARGS \
+  py::arg("size"), py::arg("num_interleaves") = 1, py::arg("preallocate_size") = 0, py::arg("device") = py::none()
 
 PYBIND11_MODULE(_C, m) {
   m.doc() = "B200-native rANS entropy coding (drop-in for torch_ans._C).";

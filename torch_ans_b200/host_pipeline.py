@@ -97,6 +97,33 @@ class HostStreamCoder:
         """Push every row of (B, N) pinned host ``symbols`` with ``indexes`` onto a fresh stream and
         return the concatenated bitstream (uint8 pinned host tensor; a view into a buffer that the
         next ``encode`` call reuses)."""
+        return self.container_to_host(self.encode_to_device(symbols, indexes))
+
+    def container_to_host(self, stream: torch.Tensor) -> torch.Tensor:
+        """Assemble the concatenated bitstream of the device stream rows ``stream`` (merge_bytes of
+        rans_stream_to_byte_strings) on the device and copy it to pinned host memory (a view into
+        a buffer that the next call reuses)."""
+        dev = self.device
+        with torch.cuda.device(dev):
+            comp = self.s_comp
+            with torch.cuda.stream(comp):
+                packed = _C.stream_to_merged_tensor(stream, self.prefix, None)
+                done = torch.cuda.Event()
+                done.record(comp)
+            total = packed.numel()
+            if self._host_out.numel() < total:
+                self._host_out = torch.empty(int(total * 1.1) + 4096, dtype=torch.uint8, pin_memory=True)
+            out = self._host_out[:total]
+            self.s_d2h.wait_event(done)
+            with torch.cuda.stream(self.s_d2h):
+                out.copy_(packed, non_blocking=True)
+            self.s_d2h.synchronize()
+            del packed
+        return out
+
+    def encode_to_device(self, symbols: torch.Tensor, indexes: torch.Tensor) -> torch.Tensor:
+        """The push half of ``encode``: returns the (B, W) device stream rows, ready on this coder's
+        compute stream (``container_to_host`` orders itself after it)."""
         if symbols.shape != indexes.shape or symbols.dim() != 2:
             raise ValueError("symbols and indexes must be 2-D with the same shape")
         for t in (symbols, indexes):
@@ -150,20 +177,10 @@ class HostStreamCoder:
                                    self.status.data_ptr(), comp.cuda_stream)
                 self._check(rc, "push")
                 ev_free[sl].record(comp)
-            with torch.cuda.stream(comp):
-                packed = _C.stream_to_merged_tensor(stream, self.prefix, None)
-                done = torch.cuda.Event()
-                done.record(comp)
-            total = packed.numel()
-            if self._host_out.numel() < total:
-                self._host_out = torch.empty(int(total * 1.1) + 4096, dtype=torch.uint8, pin_memory=True)
-            out = self._host_out[:total]
-            self.s_d2h.wait_event(done)
-            with torch.cuda.stream(self.s_d2h):
-                out.copy_(packed, non_blocking=True)
-            self.s_d2h.synchronize()
-            del packed, stream, bufs
-        return out
+            # the chunk buffers are freed on the caller's stream: order that after the last push
+            torch.cuda.current_stream(dev).wait_stream(comp)
+            del bufs
+        return stream
 
     # ------------------------------------------------------------------ decode
     def decode(self, data: torch.Tensor, indexes: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:

@@ -280,6 +280,8 @@ class TorchANSInterface(TorchEntropyCoderBaseInterface):
     def _init_stream(self, num_parallel_states=None, **kwargs) -> torch.Tensor:
         n = num_parallel_states if num_parallel_states is not None else self.num_parallel_states
         n = int(n) if n is not None else 1
+        if self.device.type == "cuda":  # made on the device: the first push needs no device read
+            return self.ans_init_func(n, device=str(self.device))
         return self._init_tensor(self.ans_init_func(n))
 
     def init_params(self, freqs, num_freqs, offsets) -> None:

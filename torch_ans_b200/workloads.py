@@ -130,7 +130,11 @@ def laplace64(device="cuda", scale: float = 1.0, length_scale: float = 1.0, seed
                     torch.zeros(K, dtype=torch.int32, device=device))
 
 
-def gaussian_latent(device="cuda", scale: float = 1.0, clamp: bool = True, seed: int = 1) -> Workload:
+def gaussian_latent(device="cuda", scale: float = 1.0, clamp: bool = True, seed: int = 1,
+                    outliers: float = 0.0) -> Workload:
+    """``outliers``: fraction of symbols replaced by values 1..3,000 beyond their table's tail (either
+    side), so that escape coding runs on these tables (without it a value past the 1e-9 tail is
+    all but absent)."""
     fp, K = 16, 64
     nb = max(1, int(16 * scale))
     g = _gen("cpu", seed)
@@ -158,6 +162,11 @@ def gaussian_latent(device="cuda", scale: float = 1.0, clamp: bool = True, seed:
     if clamp:
         t_of = tails[idx]
         sym = torch.maximum(torch.minimum(sym, t_of), -t_of)
+    if outliers > 0:
+        pick = torch.rand(shape, dtype=torch.float64, generator=g) < outliers
+        beyond = torch.randint(1, 3001, shape, generator=g, dtype=torch.int64)
+        side = torch.where(torch.rand(shape, dtype=torch.float64, generator=g) < 0.5, -1, 1)
+        sym = torch.where(pick, side * (tails[idx] + beyond), sym)
     B = nb
     sym = sym.reshape(B, -1).to(torch.int32)
     idx = idx.reshape(B, -1).to(torch.int32)
@@ -166,9 +175,11 @@ def gaussian_latent(device="cuda", scale: float = 1.0, clamp: bool = True, seed:
                     extra={"clamp": clamp})
 
 
-def zipf_alias(device="cuda", scale: float = 1.0, length_scale: float = 1.0, seed: int = 2, alias: bool = True) -> Workload:
-    from torch_ans_b200 import _C
-
+def zipf_alias(device="cuda", scale: float = 1.0, length_scale: float = 1.0, seed: int = 2, alias: bool = True,
+               alias_builder=None) -> Workload:
+    """``alias_builder``: the ``rans_alias_build_table(cdfs, cdfs_sizes, symbol_precision,
+    freq_precision)`` that makes the alias tables (CPU tensors in, CPU tensors out); by default
+    this library's.  The reference CPU leg of the benchmark passes the reference's own."""
     fp, A = 15, 4096
     B, N = max(1, int(1024 * scale)), max(1, int(1048576 * length_scale))
     p = 1.0 / torch.arange(1, A + 1, dtype=torch.float64) ** 1.1
@@ -178,7 +189,10 @@ def zipf_alias(device="cuda", scale: float = 1.0, length_scale: float = 1.0, see
     gd = _gen(device, seed)
     idx = torch.zeros((B, N), dtype=torch.int32, device=device)
     sym = _sample(cdf.to(device), inv.to(device), idx, fp, gd)
-    remap, table = _C.rans_alias_build_table(cdf, sizes, symbol_precision=12, freq_precision=fp)
+    if alias_builder is None:
+        from torch_ans_b200 import _C
+        alias_builder = _C.rans_alias_build_table
+    remap, table = alias_builder(cdf, sizes, symbol_precision=12, freq_precision=fp)
     w = Workload("zipf_alias", "rans32_16", fp, False, 4,
                  "rans32_16_alias_push" if alias else "rans32_16_push",
                  "rans32_16_alias_pop" if alias else "rans32_16_pop", sym, idx, cdf.to(device),
