@@ -98,9 +98,12 @@ int tans_push(int variant, int use_alias, int num_interleaves,
  * buffers they are handed, serving loops that must not allocate after start-up).  This entry
  * point has no counterpart in the reference.  Arguments and results are those of tans_push; the
  * encode-table scratch comes from a fixed 8 MiB array inside the library (held on every GPU that
- * loads it until the process exits), so the table list must satisfy
- * tans_push_workspace_size(variant, num_tables, cdf_width) <= 8 MiB (about 524,000 table
- * entries), else TANS_E_TOO_LARGE is returned and nothing runs.  The first call on a device looks
+ * loads it until the process exits).  The scratch a table list needs is 16 bytes per table plus
+ * 16 bytes per table entry, with min(cdf_width - 1, 2^freq_precision + 1) entries per table, each
+ * part rounded up to 256 bytes (tans_push_workspace_size gives the same figure while
+ * cdf_width <= 2^freq_precision + 2); it must be at most 8 MiB (about 524,000 table entries), else
+ * TANS_E_TOO_LARGE is returned and nothing runs.  Invalid arguments are reported first, with the
+ * codes tans_push returns.  The first call on a device looks
  * up the array's device address (cudaGetSymbolAddress); make that first call before any stream
  * capture.  All calls share the array: calls whose GPU work may overlap (different streams,
  * unordered threads) must be serialised by the caller. */

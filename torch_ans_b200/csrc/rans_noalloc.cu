@@ -56,7 +56,11 @@ extern "C" int tans_push_noalloc(int variant, int use_alias, int num_interleaves
                                  int64_t num_symbols, const int32_t* cdfs, int64_t num_tables, int64_t cdf_width,
                                  const int32_t* cdf_sizes, const int32_t* offsets, int freq_precision,
                                  int bypass_coding, int bypass_precision, uint32_t* dev_status, void* cuda_stream) {
-  if (num_tables < 0 || cdf_width < 0 || freq_precision < 1 || freq_precision > 31) return TANS_E_INVALID_ARGUMENT;
+  // the arguments are checked first, so a call gets the same error code as from tans_push
+  const int arc = tans::check_coding_args(variant, num_interleaves, stream, batch, stream_width, indexes, num_symbols,
+                                          cdfs, num_tables, cdf_width, cdf_sizes, freq_precision, bypass_coding,
+                                          bypass_precision);
+  if (arc != TANS_OK) return arc;
   const size_t need = tans::push_workspace_bytes(variant, num_tables, tans::push_entry_stride(cdf_width, freq_precision));
   if (need > kNoAllocScratchBytes) return TANS_E_TOO_LARGE;
   void* scratch = nullptr;

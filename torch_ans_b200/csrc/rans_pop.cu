@@ -720,7 +720,7 @@ int pop_impl(int variant, int lookup, int interleave, int32_t* stream, int64_t b
   if (use_l1) need += align_up((size_t)level1_bytes(ntables, fp));
   void* ws = workspace;
   bool owned = false;
-  if (!ws) {
+  if (!ws && need > 0) {  // an empty table list needs no scratch at all
     if (!allow_alloc) return TANS_E_WORKSPACE;
     if (cudaMallocAsync(&ws, need, s) != cudaSuccess) return TANS_E_CUDA;
     owned = true;

@@ -87,7 +87,8 @@ __device__ __forceinline__ void popf_stage_begin(const PopParams& P, uint32_t* t
   }
 }
 
-// wait for the staged tables; false when the wait ran out (the caller reports TANS_DEV_STALLED)
+// wait for the staged tables; false when the wait ran out.  Callers combine the result over the
+// block (__syncthreads_and) and, when any thread gave up, call popf_stage_drain before leaving.
 template <int TM>
 __device__ __forceinline__ bool popf_stage_end(unsigned long long* bar, const int* use_tma) {
   if constexpr (TM == TM_FUSED_SMEM || TM == TM_SPLIT_SMEM) {
@@ -98,6 +99,15 @@ __device__ __forceinline__ bool popf_stage_end(unsigned long long* bar, const in
   } else {
     return true;
   }
+}
+
+// After a wait that ran out: wait once more, again bounded, for the bulk copies to land, so that no
+// copy is still writing the block's shared memory when its threads leave; then report the stall.
+template <int TM>
+__device__ __forceinline__ void popf_stage_drain(unsigned long long* bar, const int* use_tma, uint32_t* status) {
+  popf_stage_end<TM>(bar, use_tma);
+  __syncthreads();
+  if (threadIdx.x == 0) report(status, DEV_STALLED);
 }
 
 template <int V> struct FastCursor {
@@ -214,10 +224,9 @@ __global__ void __launch_bounds__(512) pop_fast_kernel(const PopParams P) {
     tsm[k] = ti;
     tsm2[k] = make_int2(ti.offset, ti.size - 2);
   }
-  const bool staged = popf_stage_end<TM>(&stage_bar, &stage_tma);
-  __syncthreads();
+  const bool staged = __syncthreads_and(popf_stage_end<TM>(&stage_bar, &stage_tma) ? 1 : 0) != 0;
   if (!staged) {
-    if (threadIdx.x == 0) report(P.status, DEV_STALLED);
+    popf_stage_drain<TM>(&stage_bar, &stage_tma, P.status);
     return;
   }
   if (lane >= P.lanes) return;

@@ -85,10 +85,9 @@ __global__ void __launch_bounds__(512) pop_lean_kernel(const __grid_constant__ P
     tsm[k] = ti;
     tsm2[k] = make_int2(ti.offset, BYPASS ? ti.size - 2 : -1);
   }
-  const bool staged = popf_stage_end<TM>(&stage_bar, &stage_tma);
-  __syncthreads();
+  const bool staged = __syncthreads_and(popf_stage_end<TM>(&stage_bar, &stage_tma) ? 1 : 0) != 0;
   if (!staged) {
-    if (threadIdx.x == 0) report(P.status, DEV_STALLED);
+    popf_stage_drain<TM>(&stage_bar, &stage_tma, P.status);
     return;
   }
   if (lane >= P.lanes) return;
@@ -372,10 +371,10 @@ __global__ void __maxnreg__(96) pop_bucket_kernel(const __grid_constant__ PopPar
   }
   if (tid == 0) tsm2[P.ntables] = make_int2(0, -1);
   bool staged = true;
-  if constexpr (FUSED) staged = popf_stage_end<TM_FUSED_SMEM>(&stage_bar, &stage_tma);
+  if constexpr (FUSED) staged = __syncthreads_and(popf_stage_end<TM_FUSED_SMEM>(&stage_bar, &stage_tma) ? 1 : 0) != 0;
   const bool use_off = __syncthreads_or(any_off) != 0;
   if (!staged) {
-    if (tid == 0) report(P.status, DEV_STALLED);
+    popf_stage_drain<TM_FUSED_SMEM>(&stage_bar, &stage_tma, P.status);
     return;
   }
   if (lane >= P.lanes) return;

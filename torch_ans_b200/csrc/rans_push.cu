@@ -333,8 +333,9 @@ static int push_kernel_choice() {
 }
 
 int64_t push_entry_stride(int64_t cdf_width, int fp) {
-  // entries exist for v < cdf_width - 1, and no usable table has more than 2^fp + 1 symbols
-  const int64_t a = cdf_width - 1, b = ((int64_t)1 << fp) + 1;
+  // entries exist for v < cdf_width - 1, and no usable table has more than 2^fp + 1 symbols;
+  // an empty row (cdf_width 0 or 1) has no entries
+  const int64_t a = cdf_width > 1 ? cdf_width - 1 : 0, b = ((int64_t)1 << fp) + 1;
   return a < b ? a : b;
 }
 
@@ -351,7 +352,7 @@ int push_impl(int variant, int use_alias, int interleave, int32_t* stream, int64
   const size_t need = push_workspace_bytes(variant, ntables, stride);
   void* ws = workspace;
   bool owned = false;
-  if (!ws) {
+  if (!ws && need > 0) {  // an empty table list needs no scratch at all
     if (!allow_alloc) return TANS_E_WORKSPACE;
     if (cudaMallocAsync(&ws, need, s) != cudaSuccess) return TANS_E_CUDA;
     owned = true;
@@ -421,6 +422,8 @@ int push_impl(int variant, int use_alias, int interleave, int32_t* stream, int64
       const int blocks = (int)((batch + sb - 1) / sb);
       const size_t smem = (size_t)(fixed + sb * per);
       P.lanes = (int)lanes;
+      const int wl = env_int("TORCH_ANS_B200_WAIT_LIMIT", -1);
+      P.wait_limit = wl >= 0 ? (unsigned)wl : WS_WAIT_LIMIT;
       bool ok;
       if (variant == TANS_RANS64)
         ok = launch_push_ws<0>(P, use_alias != 0, bypass != 0, rsmem, blocks, (int)((cw + pw) * 32), (int)sb, (int)cw, smem, s);

@@ -27,6 +27,7 @@ struct PushParams {
   int lanes;
   int vec;
   int tin_smem;  // per-table info staged in shared memory
+  unsigned wait_limit;  // tries of each bounded hand-over wait (warp-specialised kernel)
 };
 
 // ---------------------------------------------------------------- step pieces

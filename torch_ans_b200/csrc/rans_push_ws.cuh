@@ -33,7 +33,9 @@ constexpr int WS_R = 4;           // entry ring slots
 constexpr int WS_D = 2;           // groups of raw symbols/indexes in flight ahead of the prep
 constexpr int WS_RR = WS_D + 2;   // raw ring slots
 // tries before a wait gives up: at least ~25 ms even when every try returns at once, far beyond
-// any real hand-over (a few microseconds)
+// any real hand-over (a few microseconds).  The launch passes it as PushParams::wait_limit; the
+// diagnostic variable TORCH_ANS_B200_WAIT_LIMIT sets another count (failure-detection tests use 0:
+// the first wait of each warp gives up at once and the block leaves through the stall path).
 constexpr unsigned WS_WAIT_LIMIT = 1u << 20;
 constexpr int WS_HEADER = 128;    // barriers + abort flag
 
@@ -152,7 +154,7 @@ __global__ void __launch_bounds__(512) push_ws_kernel(const PushParams P, int sb
     bool stalled = false;
     for (int g = 0; g < ngr; ++g) {
       const int slot = g % WS_R;
-      if (!warp_wait(full + slot, (unsigned)(g / WS_R) & 1u, abort_flag, WS_WAIT_LIMIT)) {
+      if (!warp_wait(full + slot, (unsigned)(g / WS_R) & 1u, abort_flag, P.wait_limit)) {
         stalled = true;
         break;
       }
@@ -270,13 +272,14 @@ __global__ void __launch_bounds__(512) push_ws_kernel(const PushParams P, int sb
   };
   for (int gr = 0; gr < WS_D; ++gr) issue_raw(gr);
   bool stalled = false;
+  int g_done = 0;  // groups this thread has arrived on
   for (int g = 0; g < ngr; ++g) {
     // raw group g: committed WS_D calls ago; 2 (WS_D - 1) younger groups may still be in flight
     if (g < WS_D - 1) cp_async_wait<0>();
     else cp_async_wait<2 * (WS_D - 1)>();
     const int slot = g % WS_R;
     __syncwarp();
-    if (g >= WS_R && !warp_wait(empty + slot, ((unsigned)(g / WS_R) & 1u) ^ 1u, abort_flag, WS_WAIT_LIMIT)) {
+    if (g >= WS_R && !warp_wait(empty + slot, ((unsigned)(g / WS_R) & 1u) ^ 1u, abort_flag, P.wait_limit)) {
       stalled = true;
       break;
     }
@@ -310,12 +313,21 @@ __global__ void __launch_bounds__(512) push_ws_kernel(const PushParams P, int sb
     mbar_arrive(full + slot);
     mbar_arrive_cp_async(full + slot);
     issue_raw(g + WS_D);
+    g_done = g + 1;
   }
   if (stalled) {
     if (lane == 0) *abort_flag = 1;
     if (lane == 0) report(P.status, DEV_STALLED);
   }
   cp_async_wait<0>();
+  if (*abort_flag) {
+    // the chain warps may have left already: before this thread leaves, wait (bounded) until the
+    // arrivals its copies trigger on the last groups' full barriers have landed, so that none of
+    // them reaches the block's shared memory after the block is gone
+    for (int g2 = g_done > WS_R ? g_done - WS_R : 0; g2 < g_done; ++g2)
+      for (unsigned it = 0; it < (1u << 16) && !mbar_try_wait(full + g2 % WS_R, (unsigned)(g2 / WS_R) & 1u); ++it) {
+      }
+  }
 }
 
 template <int V>
