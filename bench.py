@@ -428,17 +428,13 @@ def run_e2e(args, w, w_full, shards, ws, rank, dev):
                     job.create(total)
                 dist.barrier()
                 job.open()
-                state.update(total=total, lens=lens, offs=offs)
-            elif total != state["total"]:
-                raise RuntimeError("job bitstream size changed between identical steps")
-            local = coder.container_to_host(stream)
+                # this rank's byte range of the job file, page-locked: the records go straight in
+                h_in = job.map_range(start, end - start)
+                state.update(total=total, lens=lens, offs=offs, start=start, end=end, registered=job.registered)
+            elif total != state["total"] or start != state["start"]:
+                raise RuntimeError("job bitstream layout changed between identical steps")
+            data = coder.container_to_host(stream, out=h_in)  # raises unless it matches the lengths
             del stream
-            if local.numel() != end - start:
-                raise RuntimeError("this rank's records do not match the gathered lengths")
-            job.write(start, local)
-            if h_in is None or h_in.numel() < local.numel():
-                h_in = torch.empty(local.numel(), dtype=torch.uint8, pin_memory=True)
-            data = job.read(start, h_in[: end - start])
         else:
             data = coder.container_to_host(stream)
             del stream
@@ -479,10 +475,13 @@ def run_e2e(args, w, w_full, shards, ws, rank, dev):
                 ok = ok and got == struct.pack("<I", len(rec)) + rec and int(lens[g]) == len(rec)
                 checked += 1
         dist.barrier()
+        del data, h_in
         job.close(unlink=(rank == 0))
         res["job_bitstream"] = {"bytes": int(state["total"]), "records": int(B * ws), "records_checked": checked,
                                 "against": "records of the same streams pushed alone on one GPU",
-                                "collective": "all_gather of one int32 length per stream (NCCL)"}
+                                "collective": "all_gather of one int32 length per stream (NCCL)",
+                                "host_file": "shared file mapped by every rank, each rank's range page-locked"
+                                if state["registered"] else "shared file mapped by every rank (not page-locked)"}
     res["ok"] = max_over_ranks(0.0 if ok else 1.0, ws) == 0.0
     del h_sym, h_idx, h_out, coder, h_in
     ceil_s = host_link_ceiling(int(h2d), int(d2h), ws, dev)

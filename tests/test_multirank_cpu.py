@@ -136,7 +136,12 @@ def _rank_job_file(rank, ws, port, variant, B, N, path):
         dist.barrier()
         job.open()
         if mine:
-            job.write(start, torch.frombuffer(bytearray(mine), dtype=torch.uint8))
+            if rank == 0:  # rank 0 writes through the file, rank 1 through its mapped range
+                job.write(start, torch.frombuffer(bytearray(mine), dtype=torch.uint8))
+            else:
+                view = job.map_range(start, len(mine))
+                view.copy_(torch.frombuffer(bytearray(mine), dtype=torch.uint8))
+                del view
         dist.barrier()
         if rank == 0:
             whole = job.read(0, torch.empty(total, dtype=torch.uint8)).numpy().tobytes()

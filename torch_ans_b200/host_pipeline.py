@@ -99,10 +99,11 @@ class HostStreamCoder:
         next ``encode`` call reuses)."""
         return self.container_to_host(self.encode_to_device(symbols, indexes))
 
-    def container_to_host(self, stream: torch.Tensor) -> torch.Tensor:
+    def container_to_host(self, stream: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
         """Assemble the concatenated bitstream of the device stream rows ``stream`` (merge_bytes of
-        rans_stream_to_byte_strings) on the device and copy it to pinned host memory (a view into
-        a buffer that the next call reuses)."""
+        rans_stream_to_byte_strings) on the device and copy it to host memory: into ``out`` (a
+        uint8 host tensor of exactly the container's size, page-locked for an asynchronous copy)
+        when given, else into a pinned buffer that the next call reuses (the returned view)."""
         dev = self.device
         with torch.cuda.device(dev):
             comp = self.s_comp
@@ -111,9 +112,13 @@ class HostStreamCoder:
                 done = torch.cuda.Event()
                 done.record(comp)
             total = packed.numel()
-            if self._host_out.numel() < total:
-                self._host_out = torch.empty(int(total * 1.1) + 4096, dtype=torch.uint8, pin_memory=True)
-            out = self._host_out[:total]
+            if out is not None:
+                if out.numel() != total or out.dtype != torch.uint8 or out.is_cuda:
+                    raise ValueError(f"out must be a uint8 host tensor of {total} bytes")
+            else:
+                if self._host_out.numel() < total:
+                    self._host_out = torch.empty(int(total * 1.1) + 4096, dtype=torch.uint8, pin_memory=True)
+                out = self._host_out[:total]
             self.s_d2h.wait_event(done)
             with torch.cuda.stream(self.s_d2h):
                 out.copy_(packed, non_blocking=True)

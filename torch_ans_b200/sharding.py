@@ -130,14 +130,17 @@ def rank_byte_range(data: torch.Tensor, rows_per_rank: List[int], rank: int, num
 class JobBitstream:
     """The job-wide concatenated bitstream as one host file that every rank of the node opens.
 
-    Rank 0 creates it with the job's total size (known to every rank after the length all-gather),
-    each rank writes its records at its own offset (``write``) and reads its byte range back for
-    decoding (``read``).  ``path`` must be the same on every rank (broadcast it).  The file lives
-    in /dev/shm when that has room (host memory), else in the temporary directory."""
+    Rank 0 creates it with the job's total size (known to every rank after the length all-gather).
+    Each rank then either maps its own byte range (``map_range``: a uint8 tensor over the shared
+    pages, page-locked for the GPU when the driver accepts the registration, so device copies go
+    straight in and out of the job bitstream) or writes and reads it with ``write`` / ``read``.
+    ``path`` must be the same on every rank (broadcast it).  The file lives in /dev/shm when that
+    has room (host memory), else in the temporary directory."""
 
     def __init__(self, path: str):
         self.path = path
         self.fd = None
+        self._maps = []
 
     @staticmethod
     def default_path(tag: str, size_hint: int) -> str:
@@ -178,7 +181,35 @@ class JobBitstream:
             done += n
         return out
 
+    def map_range(self, offset: int, length: int) -> torch.Tensor:
+        """A uint8 tensor over bytes [offset, offset + length) of the file, shared with every rank
+        that maps them.  The pages are registered with the CUDA driver (page-locked) when possible,
+        so copies between the tensor and a GPU run asynchronously at full host-link speed;
+        ``registered`` tells whether that succeeded."""
+        import mmap
+        page = mmap.ALLOCATIONGRANULARITY
+        lo = (int(offset) // page) * page
+        n = int(offset) + int(length) - lo
+        mm = mmap.mmap(self.fd, max(n, 1), mmap.MAP_SHARED, mmap.PROT_READ | mmap.PROT_WRITE, offset=lo)
+        whole = torch.frombuffer(mm, dtype=torch.uint8)
+        registered = False
+        if torch.cuda.is_available() and n > 0:
+            rc = torch.cuda.cudart().cudaHostRegister(whole.data_ptr(), n, 0)
+            registered = int(rc) == 0
+        self._maps.append((mm, whole, registered))
+        self.registered = registered
+        return whole[int(offset) - lo: int(offset) - lo + int(length)]
+
     def close(self, unlink: bool = False) -> None:
+        while self._maps:
+            mm, whole, registered = self._maps.pop()
+            if registered:
+                torch.cuda.cudart().cudaHostUnregister(whole.data_ptr())
+            del whole
+            try:
+                mm.close()
+            except BufferError:  # a caller still holds a view; the mapping closes with the last one
+                pass
         if self.fd is not None:
             os.close(self.fd)
             self.fd = None
