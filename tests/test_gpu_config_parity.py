@@ -25,7 +25,7 @@ pytestmark = pytest.mark.gpu
 FIX = CC.load_fixture()
 RECT = [c.name for c in CC.CASES if c.builder != "ragged_adaptive"]
 PUSH_KERNELS = ["default", "ws", "chunk", "generic"]
-POP_VARIANTS = ["default", "lean_l1", "lean_bucket", "lean_split", "fast", "generic"]
+POP_VARIANTS = ["default", "lean_l1", "lean_bucket", "lean_bucket_plain_idx", "lean_split", "fast", "generic"]
 
 
 @pytest.fixture(scope="module")
@@ -64,10 +64,12 @@ def _force(monkeypatch, push_kernel, pop_variant):
         monkeypatch.setenv("TORCH_ANS_B200_POP_KERNEL", "lean")
         monkeypatch.setenv("TORCH_ANS_B200_POP_LAYOUT", "bucket_global")
         monkeypatch.setenv("TORCH_ANS_B200_POP_L1", "1")
-    elif pop_variant == "lean_bucket":
+    elif pop_variant in ("lean_bucket", "lean_bucket_plain_idx"):
         monkeypatch.setenv("TORCH_ANS_B200_POP_KERNEL", "lean")
         monkeypatch.setenv("TORCH_ANS_B200_POP_LAYOUT", "bucket_global")
         monkeypatch.setenv("TORCH_ANS_B200_POP_L1", "0")
+        if pop_variant == "lean_bucket_plain_idx":  # indexes on plain loads instead of the ring
+            monkeypatch.setenv("TORCH_ANS_B200_POP_IRING", "0")
     elif pop_variant == "lean_split":
         monkeypatch.setenv("TORCH_ANS_B200_POP_KERNEL", "lean")
         monkeypatch.setenv("TORCH_ANS_B200_POP_LAYOUT", "split_global")

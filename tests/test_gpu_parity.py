@@ -518,19 +518,22 @@ def test_pop_heavy_tails_and_overrun(C, kernel, layout, lookup, variant, monkeyp
     assert same_rows(st.cpu().numpy(), ref_pop)
 
 
+@pytest.mark.parametrize("iring", ["1", "0"])
 @pytest.mark.parametrize("l1", ["0", "1"])
 @pytest.mark.parametrize("lookup", ["search", "invcdf"])
 @pytest.mark.parametrize("variant", VARIANTS)
-def test_bucket_pop_zero_offsets_tails_and_bad_rows(C, lookup, variant, l1, monkeypatch):
+def test_bucket_pop_zero_offsets_tails_and_bad_rows(C, lookup, variant, l1, iring, monkeypatch):
     """The bucket-layout pop with every table offset zero (the kernel then skips the per-step
     offset read), a table whose last symbol covers whole buckets up to 2^fp, unit-frequency tails
     (marker buckets), bad indexes and underflow: identical to the oracle.  Then rows whose length
     points past the row's end (a corrupted length the reference would read past the row for): the
     bucket pop must agree with the generic pop kernel, which takes the same exact step, and flag
-    underflow.  With and without the level-1 table in shared memory."""
+    underflow.  With and without the level-1 table in shared memory, with the indexes through the
+    shared-memory ring fed by bulk copies and on plain loads."""
     monkeypatch.setenv("TORCH_ANS_B200_POP_KERNEL", "lean")
     monkeypatch.setenv("TORCH_ANS_B200_POP_LAYOUT", "bucket_global")
     monkeypatch.setenv("TORCH_ANS_B200_POP_L1", l1)
+    monkeypatch.setenv("TORCH_ANS_B200_POP_IRING", iring)
     rng = np.random.default_rng(zlib.crc32(f"bucket0-{lookup}-{variant}".encode()))
     fp = FP[variant]
     fp, cdfs, sizes, _ = _heavy_tail_case(rng, K=5, A=300, fp=fp)
@@ -576,6 +579,38 @@ def test_bucket_pop_zero_offsets_tails_and_bad_rows(C, lookup, variant, l1, monk
     assert np.array_equal(outs["lean"][1], outs["generic"][1])
     # the rows with intact lengths decode as before
     assert np.array_equal(outs["lean"][0][1::4], sym[1::4])
+
+
+@pytest.mark.parametrize("nchunks", [1, 2, 16, 17, 33])
+@pytest.mark.parametrize("iring", ["1", "0"])
+@pytest.mark.parametrize("variant", VARIANTS)
+def test_bucket_pop_short_rows_and_ring_boundaries(C, variant, iring, nchunks, monkeypatch):
+    """Rows of 1, 2, 16, 17 and 33 chunks of four symbols: the index ring's first fill, its
+    half boundaries (16 chunks per half) and its refills at the row's end, against the oracle."""
+    monkeypatch.setenv("TORCH_ANS_B200_POP_KERNEL", "lean")
+    monkeypatch.setenv("TORCH_ANS_B200_POP_LAYOUT", "bucket_global")
+    monkeypatch.setenv("TORCH_ANS_B200_POP_L1", "0")
+    monkeypatch.setenv("TORCH_ANS_B200_POP_IRING", iring)
+    rng = np.random.default_rng(zlib.crc32(f"ring-{variant}-{nchunks}".encode()))
+    fp = FP[variant]
+    fp, cdfs, sizes, offs = _heavy_tail_case(rng, K=7, A=120, fp=fp)
+    K = cdfs.shape[0]
+    B, N = 37, 4 * nchunks
+    idx = rng.integers(0, K, (B, N)).astype(np.int32)
+    sym = (rng.integers(0, sizes[idx] - 1) + offs[idx]).astype(np.int32)
+    # uniform symbols over heavy tails cost ~fp bits each: on rows this short the worst-case
+    # width rule leaves no slack, so the rows get preallocated room
+    ref, perr = O.push(variant, O.init_stream(variant, B, preallocate_size=64), sym, idx, cdfs, sizes, offs, fp,
+                       False)
+    assert perr == 0
+    st = t(ref)
+    dec = getattr(C, f"{variant}_pop")(st, t(idx), t(cdfs), t(sizes), t(offs), freq_precision=fp,
+                                       bypass_coding=False)
+    assert C.device_status() == 0
+    assert np.array_equal(dec.cpu().numpy(), sym)
+    ref_pop = ref.copy()
+    O.pop(variant, ref_pop, idx, cdfs, sizes, offs, fp, False)
+    assert same_rows(st.cpu().numpy(), ref_pop)
 
 
 @pytest.mark.parametrize("l1", ["0", "1"])

@@ -242,6 +242,12 @@ __device__ __forceinline__ void bulk_copy_g2s(void* smem, const void* gmem, unsi
                : "memory");
 }
 
+// orders this thread's earlier generic-proxy accesses of shared memory before its later
+// async-proxy (bulk copy) accesses: needed before a bulk copy overwrites data the thread read
+__device__ __forceinline__ void fence_proxy_async_shared() {
+  asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+}
+
 // L2 eviction policies: tables that every step reads stay (evict_last); data read or written
 // once goes first (evict_first), so streaming rows do not push the tables out of L2.
 __device__ __forceinline__ unsigned long long policy_evict_last() {

@@ -707,6 +707,20 @@ int pop_impl(int variant, int lookup, int interleave, int32_t* stream, int64_t b
     use_l1 = (int64_t)smem + 16 + l1b <= kSmemBudget && (env_l1 == 1 || (env_l1 != 0 && batch <= 2 * (int64_t)dev_sms));
     if (use_l1) smem += 16 + (size_t)l1b;
   }
+  // index ring of the bucket kernel (its bucket and fused-shared launches): per stream two halves
+  // of kRingChunks index chunks and two mbarriers, after everything else in shared memory, when
+  // it fits (TORCH_ANS_B200_POP_IRING=0 keeps the indexes on plain loads)
+  int64_t iring_off = 0;
+  bool iring = false;
+  if (lean && (tm == TM_BUCKET_GLOBAL || tm == TM_FUSED_SMEM) && env_int("TORCH_ANS_B200_POP_IRING", 1) != 0) {
+    const int64_t nsl = (int64_t)(L.threads / 32) * L.lanes;
+    const int64_t off = ((int64_t)smem + 15) & ~(int64_t)15;
+    if (off + nsl * kRingBytesPerStream <= kSmemBudget) {
+      iring = true;
+      iring_off = off;
+      smem = (size_t)(off + nsl * kRingBytesPerStream);
+    }
+  }
   const bool fast = tm >= 0;
   const bool need_fused = fast ? (tm == TM_FUSED_SMEM || tm == TM_FUSED_GLOBAL)
                                : (use_tables && ov != 100 && fused_bytes(ntables, fp) <= kFusedMaxBytes);
@@ -811,6 +825,8 @@ int pop_impl(int variant, int lookup, int interleave, int32_t* stream, int64_t b
     P.lanes = L.lanes;
     P.tin_smem = tin_smem ? 1 : 0;
     P.spt = spt;
+    P.iring = iring ? 1 : 0;
+    P.iring_off = iring_off;
     bool launched;
     if (lean) {
       if (variant == TANS_RANS64) launched = launch_pop_lean<0>(P, lookup, bypass != 0, tm, L.blocks, L.threads, smem, s);

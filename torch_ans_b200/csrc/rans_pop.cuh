@@ -36,6 +36,8 @@ struct PopParams {
   int fused_smem;      // fused table staged in shared memory
   int tin_smem;        // per-table info staged in shared memory
   int vec_out;         // out is 16-byte aligned
+  int iring;           // bucket kernel: indexes through a per-stream shared-memory ring fed by bulk copies
+  int64_t iring_off;   // its byte offset in the block's dynamic shared memory
 };
 
 template <int V> struct PopCursor {
@@ -91,6 +93,13 @@ __device__ __noinline__ int32_t pop_escape(typename VT<V>::State& x, PopCursor<V
 }
 
 enum : int { LK_SEARCH = 0, LK_INVCDF = 1, LK_ALIAS = 2 };
+
+// bucket kernel's index ring: two halves of kRingChunks chunks (4 indexes each) per stream, plus
+// two 8-byte mbarriers per stream
+constexpr int kRingChunks = 16;
+constexpr int64_t kRingBytesPerStream = 2 * kRingChunks * 16 + 16;
+// tries of a ring wait before it gives up (TANS_DEV_STALLED): far beyond any real copy
+constexpr unsigned kRingWaitLimit = 1u << 20;
 
 // a table word: read-only global memory (GLOBAL) or a row staged in shared memory
 template <bool GLOBAL> __device__ __forceinline__ int32_t ldrow(const int32_t* p) {

@@ -332,7 +332,7 @@ __device__ __forceinline__ uint32_t ld_word_if(const uint8_t* p, bool pred, uint
 // table modes of pop_bucket_kernel
 enum : int { BM_L2 = 0, BM_L1 = 1, BM_FUSED = 2 };
 
-template <int V, int LK, bool BYPASS, int MODE>
+template <int V, int LK, bool BYPASS, int MODE, bool IRING>
 __global__ void __maxnreg__(96) pop_bucket_kernel(const __grid_constant__ PopParams P) {
   using S = typename VT<V>::State;
   using W = typename VT<V>::Word;
@@ -452,20 +452,83 @@ __global__ void __maxnreg__(96) pop_bucket_kernel(const __grid_constant__ PopPar
     }
   } else {
     // indexes two chunks (eight steps) ahead: kn0 holds chunk c + 1, kn1 chunk c + 2 (the copy
-    // kn0 = kn1 reads a load issued a whole chunk earlier)
-    int4 kn0 = nch > 0 ? ld_idx4(irow, pol_stream) : make_int4(0, 0, 0, 0);
-    int4 kn1 = nch > 1 ? ld_idx4(irow + 4, pol_stream) : make_int4(0, 0, 0, 0);
+    // kn0 = kn1 reads a load issued a whole chunk earlier).
+    // IRING: the indexes come from shared memory instead.  This lane keeps its stream's indexes in
+    // a two-half ring of kRingChunks-chunk tiles; a half is filled by one 1D bulk copy (copy
+    // engine, completing on the half's mbarrier) issued a whole half ahead of its first read.
+    // Measured on this path: an index load through the load pipeline delays the table-entry loads
+    // behind it by ~40 cycles per step; the ring's reads are shared-memory loads.
+    int4* ring = nullptr;
+    unsigned long long* ibar = nullptr;
+    uint32_t wpar = 0;  // bit h: parity of the next phase of half h
+    uint32_t pend = 0;  // bit h: a copy into half h is in flight
+    auto ring_issue = [&](int h, int start) {
+      const int n = min(kRingChunks, nch - start);
+      if (n > 0) {
+        mbar_arrive_expect_tx(ibar + h, (unsigned)n * 16u);
+        bulk_copy_g2s(ring + h * kRingChunks, irow + 4 * (int64_t)start, (unsigned)n * 16u, ibar + h);
+        pend |= 1u << h;
+      }
+    };
+    auto ring_wait = [&](int h) -> bool {
+      const unsigned par = (wpar >> h) & 1u;
+      for (unsigned it = 0; it < kRingWaitLimit; ++it)
+        if (mbar_try_wait(ibar + h, par)) {
+          wpar ^= 1u << h;
+          pend &= ~(1u << h);
+          return true;
+        }
+      err |= DEV_STALLED;
+      return false;
+    };
+    bool dead = false;  // a ring wait ran out: the stream stops
+    if constexpr (IRING) {
+      const int sl = warp * P.lanes + lane, nsl = warps * P.lanes;
+      ring = reinterpret_cast<int4*>(smem_raw + P.iring_off) + (size_t)sl * 2 * kRingChunks;
+      ibar = reinterpret_cast<unsigned long long*>(smem_raw + P.iring_off + (size_t)nsl * 2 * kRingChunks * 16) +
+             2 * sl;
+      mbar_init(ibar, 1u);
+      mbar_init(ibar + 1, 1u);
+      mbar_init_fence();
+      ring_issue(0, 0);
+      ring_issue(1, kRingChunks);
+      if (pend & 1u) dead = !ring_wait(0);  // nothing was issued for an empty row
+    }
+    int4 kn0 = make_int4(0, 0, 0, 0), kn1 = make_int4(0, 0, 0, 0);
+    if constexpr (IRING) {
+      kn0 = ring[0];
+      kn1 = ring[1];
+    } else {
+      if (nch > 0) kn0 = ld_idx4(irow, pol_stream);
+      if (nch > 1) kn1 = ld_idx4(irow + 4, pol_stream);
+    }
     uintptr_t a = addr_of(row_of(kn0.x), (uint32_t)x);
     // the entry of the next step: each step issues the next step's load before its own rare-step
     // branch, so the branch resolves while the load is in flight (the rare step reissues it)
     unsigned long long en = load_at(a);
+    // With the ring the chunks run in halves of kRingChunks, each in two parts: the first
+    // kRingChunks - 2 chunks read indexes of this half only (two chunks ahead); then this half has
+    // been read in full, so its slots are refilled with the half after next (needed a whole half
+    // later), and the next half -- copied a whole half ago -- is waited for before the last two
+    // chunks read into it.  Without the ring there is one part over all chunks.
+    const int span = IRING ? kRingChunks : nch;
 #pragma unroll 1
-    for (int c = 0; c < nch; ++c) {
+    for (int c0 = 0; c0 < nch && !dead; c0 += span) {
+#pragma unroll 1
+    for (int part = 0; part < (IRING ? 2 : 1) && !dead; ++part) {
+      const int ca = part == 0 ? c0 : c0 + kRingChunks - 2;
+      const int cb = IRING ? min(nch, part == 0 ? c0 + kRingChunks - 2 : c0 + kRingChunks) : nch;
+#pragma unroll 1
+    for (int c = ca; c < cb; ++c) {
       {
         const int4 k4 = kn0;
         kn0 = kn1;
         const int32_t knext = kn0.x;  // first index of chunk c + 1
-        if (c + 2 < nch) kn1 = ld_idx4(irow + 4 * (int64_t)(c + 2), pol_stream);
+        if constexpr (IRING) {
+          kn1 = ring[(c + 2) & (2 * kRingChunks - 1)];  // past the row's end: a stale entry, unused
+        } else {
+          if (c + 2 < nch) kn1 = ld_idx4(irow + 4 * (int64_t)(c + 2), pol_stream);
+        }
         const int32_t kv[5] = {k4.x, k4.y, k4.z, k4.w, knext};
         // table offsets (and escape slots) of the chunk's four steps, read only when some table
         // has an offset or escapes are coded (a block-uniform branch, once per chunk)
@@ -605,6 +668,21 @@ __global__ void __maxnreg__(96) pop_bucket_kernel(const __grid_constant__ PopPar
         st_hint_v4(reinterpret_cast<int4*>(orow + 4 * (int64_t)c), make_int4(ov[0], ov[1], ov[2], ov[3]), pol_stream);
       }
     }
+      if (IRING && part == 0) {
+        const int h = (c0 / kRingChunks) & 1;
+        if (c0 + 2 * kRingChunks < nch) {
+          fence_proxy_async_shared();  // this half's reads come before the copy over it
+          ring_issue(h, c0 + 2 * kRingChunks);
+        }
+        if (c0 + kRingChunks < nch && !ring_wait(h ^ 1)) dead = true;
+      }
+    }
+    }
+    // after a wait that ran out, let the copies still in flight land (bounded) before leaving
+    if constexpr (IRING) {
+      for (int h = 0; h < 2; ++h)
+        if (pend & (1u << h)) ring_wait(h);
+    }
     if (p < p_init && p + 1 < first) err |= DEV_UNDERFLOW;
   }
   store_state<V>(row, 0, x);
@@ -616,12 +694,18 @@ template <int V>
 bool launch_pop_lean(const PopParams& P, int lookup, bool bypass, int tm, int blocks, int threads, size_t smem,
                      cudaStream_t s);
 
+template <int V, int LK, bool BY, int MODE, bool IR>
+void popb_go2(const PopParams& P, int blocks, int threads, size_t smem, cudaStream_t s) {
+  if (smem > 48 * 1024)
+    cudaFuncSetAttribute(pop_bucket_kernel<V, LK, BY, MODE, IR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)smem);
+  pop_bucket_kernel<V, LK, BY, MODE, IR><<<blocks, threads, smem, s>>>(P);
+  note_launch();
+}
 template <int V, int LK, bool BY, int MODE>
 void popb_go1(const PopParams& P, int blocks, int threads, size_t smem, cudaStream_t s) {
-  if (smem > 48 * 1024)
-    cudaFuncSetAttribute(pop_bucket_kernel<V, LK, BY, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  pop_bucket_kernel<V, LK, BY, MODE><<<blocks, threads, smem, s>>>(P);
-  note_launch();
+  if (P.iring) popb_go2<V, LK, BY, MODE, true>(P, blocks, threads, smem, s);
+  else popb_go2<V, LK, BY, MODE, false>(P, blocks, threads, smem, s);
 }
 template <int V, int LK, bool BY>
 void popb_go(const PopParams& P, int blocks, int threads, size_t smem, cudaStream_t s) {
