@@ -475,7 +475,7 @@ def run_e2e(args, w, w_full, shards, ws, rank, dev):
                 ok = ok and got == struct.pack("<I", len(rec)) + rec and int(lens[g]) == len(rec)
                 checked += 1
         dist.barrier()
-        del data, h_in
+        h_in = None  # the last view of this rank's mapped range goes before the mapping closes
         job.close(unlink=(rank == 0))
         res["job_bitstream"] = {"bytes": int(state["total"]), "records": int(B * ws), "records_checked": checked,
                                 "against": "records of the same streams pushed alone on one GPU",

@@ -95,9 +95,12 @@ __device__ __noinline__ int32_t pop_escape(typename VT<V>::State& x, PopCursor<V
 enum : int { LK_SEARCH = 0, LK_INVCDF = 1, LK_ALIAS = 2 };
 
 // bucket kernel's index ring: two halves of kRingChunks chunks (4 indexes each) per stream, plus
-// two 8-byte mbarriers per stream
+// two 8-byte mbarriers per stream.  A stream's ring starts kRingStride bytes after the previous
+// one: 16 bytes more than the ring, so the lanes of a warp reading the same chunk slot hit
+// different shared-memory banks.
 constexpr int kRingChunks = 16;
-constexpr int64_t kRingBytesPerStream = 2 * kRingChunks * 16 + 16;
+constexpr int64_t kRingStride = 2 * kRingChunks * 16 + 16;
+constexpr int64_t kRingBytesPerStream = kRingStride + 16;
 // tries of a ring wait before it gives up (TANS_DEV_STALLED): far beyond any real copy
 constexpr unsigned kRingWaitLimit = 1u << 20;
 

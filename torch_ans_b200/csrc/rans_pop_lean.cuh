@@ -484,9 +484,8 @@ __global__ void __maxnreg__(96) pop_bucket_kernel(const __grid_constant__ PopPar
     bool dead = false;  // a ring wait ran out: the stream stops
     if constexpr (IRING) {
       const int sl = warp * P.lanes + lane, nsl = warps * P.lanes;
-      ring = reinterpret_cast<int4*>(smem_raw + P.iring_off) + (size_t)sl * 2 * kRingChunks;
-      ibar = reinterpret_cast<unsigned long long*>(smem_raw + P.iring_off + (size_t)nsl * 2 * kRingChunks * 16) +
-             2 * sl;
+      ring = reinterpret_cast<int4*>(smem_raw + P.iring_off + (size_t)sl * kRingStride);
+      ibar = reinterpret_cast<unsigned long long*>(smem_raw + P.iring_off + (size_t)nsl * kRingStride) + 2 * sl;
       mbar_init(ibar, 1u);
       mbar_init(ibar + 1, 1u);
       mbar_init_fence();
