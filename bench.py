@@ -71,6 +71,8 @@ def parse():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--parity-streams", type=int, default=64,
                     help="streams of the byte-parity sample when no CPU-baseline sample is run (N > 1)")
+    ap.add_argument("--probe", action="store_true",
+                    help="instead of the benchmark: the latency probes (cycles of one dependent step, tans_probe)")
     ap.add_argument("--clocks-dir", default=None,
                     help="folder that keeps the nvidia-smi samples of the timed region (default: a temporary folder)")
     return ap.parse_args()
@@ -784,8 +786,28 @@ def reference_arm(args, ws, rank, cfg):
             print(json.dumps(line), flush=True)
 
 
+def run_probes():
+    """The latency probes behind the kernel design: cycles of one dependent step (clock64 on the
+    device), printed as one JSON line."""
+    from torch_ans_b200 import capi
+    steps = {"smem_chase": 1 << 20, "l2_chase": 1 << 18, "l2_chase_busy": 1 << 15}
+    out = {k: capi.probe(k, steps.get(k, 1 << 20)) for k in capi.PROBES}
+    mhz = None
+    try:
+        r = subprocess.run(["nvidia-smi", "--id=0", "--query-gpu=clocks.sm", "--format=csv,noheader,nounits"],
+                           capture_output=True, text=True, timeout=20)
+        mhz = float(r.stdout.strip().splitlines()[0])
+    except Exception:
+        pass
+    print(json.dumps({"probe": "cycles per dependent step", "gpu": torch.cuda.get_device_name(0), "sm_mhz_after": mhz,
+                      "cycles": {k: round(v, 1) for k, v in out.items()}}), flush=True)
+
+
 def main():
     args = parse()
+    if args.probe:
+        run_probes()
+        return
     ws, rank, local = dist_setup()
     ragged = args.workload == "ragged_adaptive"
     cfg = {"workload": args.workload, "scale": args.scale, "length_scale": args.length_scale,

@@ -67,6 +67,28 @@ const char* tans_status_string(int code);
  * report how many of the library's kernels ran in it. */
 uint64_t tans_launch_count(void);
 
+/* Latency probes behind the kernel design: cycles of one dependent step, measured with clock64 on
+ * the device (no counterpart in the reference; a diagnostic that allocates, runs one kernel and
+ * synchronises).  kind:
+ *   TANS_PROBE_SMEM_CHASE    dependent loads around a random cycle in 48 KB of shared memory
+ *   TANS_PROBE_L2_CHASE      dependent 8-byte loads around a random cycle in an 8 MB buffer held in
+ *                            L2 (the bucket table's size), one thread
+ *   TANS_PROBE_L2_CHASE_BUSY the same with 56 chasing lanes per SM on every SM (14 warps x 4 lanes)
+ *   TANS_PROBE_POP32_STEP / TANS_PROBE_PUSH32_STEP / TANS_PROBE_POP64_STEP / TANS_PROBE_PUSH64_STEP
+ *                            the dependent instructions of one rans32 / rans64 pop or push step
+ *                            (16-bit precision, table entry in shared memory, words in registers,
+ *                            renormalising every step), one thread: the floor under a kernel that
+ *                            codes one stream per SM.
+ * *cycles_per_step receives the mean over the probe's chains. */
+#define TANS_PROBE_SMEM_CHASE 0
+#define TANS_PROBE_L2_CHASE 1
+#define TANS_PROBE_L2_CHASE_BUSY 2
+#define TANS_PROBE_POP32_STEP 3
+#define TANS_PROBE_PUSH32_STEP 4
+#define TANS_PROBE_POP64_STEP 5
+#define TANS_PROBE_PUSH64_STEP 6
+int tans_probe(int kind, int64_t steps, double* cycles_per_step);
+
 /* Bytes of device scratch that tans_push needs for a table list of num_tables rows of cdf_width
  * entries (a per-entry reciprocal table plus per-table size/offset pairs). */
 size_t tans_push_workspace_size(int variant, int64_t num_tables, int64_t cdf_width);

@@ -222,3 +222,14 @@ def test_ballot_prefix_rule_equals_reference_bisection():
                 fired += 1
                 assert bin(m).count("1") - 1 == _reference_bisection(row, size, cum, fp), (row, size, cum)
     assert fired > 1000
+
+
+def test_probe_rejects_bad_arguments_without_a_device():
+    """tans_probe checks its arguments on the host before any CUDA call."""
+    import ctypes
+    from torch_ans_b200 import capi
+    lib = capi.load()
+    out = ctypes.c_double(0.0)
+    assert lib.tans_probe(capi.PROBES["pop32_step"], 0, ctypes.byref(out)) == 1
+    assert lib.tans_probe(99, 10, ctypes.byref(out)) == 1
+    assert lib.tans_probe(0, 10, None) == 1

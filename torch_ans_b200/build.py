@@ -29,7 +29,8 @@ LIB = os.path.join(PKG, "libtorch_ans_b200.so")
 CU_SOURCES = ["rans_push.cu", "rans_pop.cu", "rans_aux.cu", "rans_pop_fast_v0.cu", "rans_pop_fast_v1.cu",
               "rans_pop_fast_v2.cu", "rans_push_fast_v0.cu", "rans_push_fast_v1.cu", "rans_push_fast_v2.cu",
               "rans_push_ws_v0.cu", "rans_push_ws_v1.cu", "rans_push_ws_v2.cu", "rans_pop_lean_v0.cu",
-              "rans_pop_lean_v1.cu", "rans_pop_lean_v2.cu", "rans_noalloc.cu", "rans_ragged.cu", "rans_alias.cu"]
+              "rans_pop_lean_v1.cu", "rans_pop_lean_v2.cu", "rans_noalloc.cu", "rans_ragged.cu", "rans_alias.cu",
+              "rans_probe.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -42,7 +42,21 @@ _SIGS = {
     "tans_push_ragged": ([_I, _P, _I64, _I64, _P, _P, _P, _I64, _P, _I64, _I64, _P, _P, _I, _I, _I, _P, _SZ, _P, _P],
                          _I),
     "tans_pop_ragged": ([_I, _P, _I64, _I64, _P, _P, _P, _I64, _P, _I64, _I64, _P, _P, _I, _I, _I, _P, _P], _I),
+    "tans_probe": ([_I, _I64, ctypes.POINTER(ctypes.c_double)], _I),
 }
+
+PROBES = {"smem_chase": 0, "l2_chase": 1, "l2_chase_busy": 2, "pop32_step": 3, "push32_step": 4, "pop64_step": 5,
+          "push64_step": 6}
+
+
+def probe(kind: str, steps: int = 200000) -> float:
+    """Cycles of one dependent step of a latency probe (tans_probe; needs a GPU)."""
+    lib = load()
+    out = ctypes.c_double(0.0)
+    rc = lib.tans_probe(PROBES[kind], int(steps), ctypes.byref(out))
+    if rc != OK:
+        raise RuntimeError(f"tans_probe({kind}): {lib.tans_status_string(rc).decode()}")
+    return out.value
 
 _lib = None
 
