@@ -138,22 +138,29 @@ def _random_case(rng, variant, bypass, K=5, A=40, fp=None):
     return fp, cdfs, sizes, offs
 
 
-@pytest.mark.parametrize("variant", VARIANTS)
-@pytest.mark.parametrize("bypass", [False, True])
-@pytest.mark.parametrize("interleave", [1, 4])
-@pytest.mark.parametrize("lookup", ["search", "invcdf", "alias"])
-@pytest.mark.parametrize("table_path", ["fused", "direct", "fused_small"])
+def _random_combos():
+    """Every op the reference has (no 4-state alias op, no rans64_i4_invcdf_pop) through every
+    table path that applies (4-state pops read the caller's tables directly in every mode)."""
+    out = []
+    for table_path in ("fused", "direct", "fused_small"):
+        for lookup in ("search", "invcdf", "alias"):
+            for interleave in (1, 4):
+                for bypass in (False, True):
+                    for variant in VARIANTS:
+                        if interleave == 4 and (lookup == "alias" or table_path != "fused" or
+                                                (lookup == "invcdf" and variant == "rans64")):
+                            continue
+                        out.append(pytest.param(variant, bypass, interleave, lookup, table_path,
+                                                id=f"{table_path}-{lookup}-{interleave}-{bypass}-{variant}"))
+    return out
+
+
+@pytest.mark.parametrize("variant,bypass,interleave,lookup,table_path", _random_combos())
 def test_random_against_oracle(C, variant, bypass, interleave, lookup, table_path, monkeypatch):
     """Seeded cases with odd lengths and misaligned rows (vector and scalar load paths), through
     each decode table path: fused table in L2 ("fused"), fused table small enough for shared
     memory ("fused_small", fp 11), and the caller's tables read directly ("direct")."""
     monkeypatch.setenv("TORCH_ANS_B200_FUSED", "0" if table_path == "direct" else "1")
-    if lookup == "alias" and interleave == 4:
-        pytest.skip("the reference has no 4-state alias op")
-    if lookup == "invcdf" and interleave == 4 and variant == "rans64":
-        pytest.skip("the reference has no rans64_i4_invcdf_pop")
-    if table_path != "fused" and interleave == 4:
-        pytest.skip("4-state pops read the caller's tables directly in every mode")
     rng = np.random.default_rng(zlib.crc32(f"{variant}-{bypass}-{interleave}-{lookup}-{table_path}".encode()))
     if lookup == "alias":
         fp = 12
@@ -284,23 +291,34 @@ def test_device_stream_helpers():
 LAYOUTS = ["fused_smem", "split_smem", "fused_global", "split_global", "bucket_global", "generic"]
 
 
-@pytest.mark.parametrize("layout", LAYOUTS)
-@pytest.mark.parametrize("variant", VARIANTS)
-@pytest.mark.parametrize("lookup", ["search", "invcdf", "alias"])
-@pytest.mark.parametrize("bypass", [False, True])
-@pytest.mark.parametrize("spt", ["1", "4"])
-@pytest.mark.parametrize("kernel", ["lean", "fast"])
+def _layout_combos():
+    """Layouts a lookup can use (alias offsets depend on cum: fused layouts only; fused_global
+    serves alias tables when several streams share a thread), streams per thread only for the
+    fast kernel (the lean one runs one stream per thread)."""
+    out = []
+    for kernel in ("lean", "fast"):
+        for spt in ("1", "4"):
+            for bypass in (False, True):
+                for lookup in ("search", "invcdf", "alias"):
+                    for variant in VARIANTS:
+                        for layout in LAYOUTS:
+                            if layout in ("split_smem", "split_global", "bucket_global") and lookup == "alias":
+                                continue
+                            if layout == "fused_global" and lookup != "alias" and spt == "4":
+                                continue
+                            if kernel == "lean" and spt == "4":
+                                continue
+                            out.append(pytest.param(layout, variant, lookup, bypass, spt, kernel,
+                                                    id=f"{kernel}-{spt}-{bypass}-{lookup}-{variant}-{layout}"))
+    return out
+
+
+@pytest.mark.parametrize("layout,variant,lookup,bypass,spt,kernel", _layout_combos())
 def test_fast_pop_layouts(C, layout, variant, lookup, bypass, spt, kernel, monkeypatch):
     """Aligned rows with a length divisible by 4 take the lean pop kernel (one stream per thread,
     shortest serial step) or the fast one (several streams per thread); every table layout they
     can use is forced in turn (an infeasible one falls back to the automatic choice) and must
     decode exactly what the oracle decodes, with the same final stream rows."""
-    if layout in ("split_smem", "split_global", "bucket_global") and lookup == "alias":
-        pytest.skip("alias offsets depend on cum: fused layouts only")
-    if layout == "fused_global" and lookup != "alias" and spt == "4":
-        pytest.skip("fused_global serves alias tables")
-    if kernel == "lean" and spt == "4":
-        pytest.skip("the lean kernel runs one stream per thread")
     monkeypatch.setenv("TORCH_ANS_B200_POP_KERNEL", kernel)
     monkeypatch.setenv("TORCH_ANS_B200_POP_LAYOUT", layout)
     monkeypatch.setenv("TORCH_ANS_B200_SPT", spt)
@@ -475,10 +493,16 @@ def _heavy_tail_case(rng, K=6, A=300, fp=16):
     return fp, cdfs, sizes, offs
 
 
-@pytest.mark.parametrize("kernel", ["lean", "lean_l1", "fast"])
-@pytest.mark.parametrize("layout", ["bucket_global", "split_global", "split_smem", "fused_smem"])
-@pytest.mark.parametrize("lookup", ["search", "invcdf"])
-@pytest.mark.parametrize("variant", VARIANTS)
+def _tail_combos():
+    """The level-1 table fronts the bucket layout only."""
+    return [pytest.param(kernel, layout, lookup, variant, id=f"{variant}-{lookup}-{layout}-{kernel}")
+            for kernel in ("lean", "lean_l1", "fast")
+            for layout in ("bucket_global", "split_global", "split_smem", "fused_smem")
+            for lookup in ("search", "invcdf") for variant in VARIANTS
+            if not (kernel == "lean_l1" and layout != "bucket_global")]
+
+
+@pytest.mark.parametrize("kernel,layout,lookup,variant", _tail_combos())
 def test_pop_heavy_tails_and_overrun(C, kernel, layout, lookup, variant, monkeypatch):
     """Unit-frequency tails (bucket entries that cannot describe their cum range, so those steps
     take the split tables or the exact step), symbols drawn uniformly over the alphabet (every
@@ -486,8 +510,6 @@ def test_pop_heavy_tails_and_overrun(C, kernel, layout, lookup, variant, monkeyp
     (underflow): outputs, final rows and error bits must all equal the oracle's.  "lean" and
     "lean_l1" run the lean kernels without and with the bucket layout's level-1 table in shared
     memory."""
-    if kernel == "lean_l1" and layout != "bucket_global":
-        pytest.skip("the level-1 table fronts the bucket layout only")
     monkeypatch.setenv("TORCH_ANS_B200_POP_KERNEL", "lean" if kernel.startswith("lean") else kernel)
     monkeypatch.setenv("TORCH_ANS_B200_POP_L1", "1" if kernel == "lean_l1" else "0")
     monkeypatch.setenv("TORCH_ANS_B200_POP_LAYOUT", layout)
