@@ -125,9 +125,11 @@ def test_zipf_alias_tables_built_on_device_match_reference(C):
     assert CC._digest(remap.cpu(), table.cpu()) == FIX["zipf_alias"]["alias_tables_sha256"]
 
 
-@pytest.mark.parametrize("warp_pop", ["1", "0"])
-def test_ragged_config_rows_match_per_stream_reference(C, warp_pop, monkeypatch):
-    monkeypatch.setenv("TORCH_ANS_B200_RAGGED_POP_WARP", warp_pop)
+@pytest.mark.parametrize("pop_kernel", ["lean", "warp", "thread"])
+def test_ragged_config_rows_match_per_stream_reference(C, pop_kernel, monkeypatch):
+    monkeypatch.setenv("TORCH_ANS_B200_RAGGED_POP_WARP", "0" if pop_kernel == "thread" else "1")
+    monkeypatch.setenv("TORCH_ANS_B200_RAGGED_POP_LEAN", "1" if pop_kernel == "lean" else "0")
+    monkeypatch.setenv("TORCH_ANS_B200_RAGGED_PUSH_LEAN", "1" if pop_kernel == "lean" else "0")
     w, rec = expected("ragged_adaptive")
     dev = torch.device("cuda")
     kw = dict(freq_precision=w.fp, bypass_coding=w.bypass, bypass_precision=w.bp)

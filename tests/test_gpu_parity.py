@@ -416,6 +416,41 @@ def test_fast_push_kernels(C, kernel, variant, alias, bypass, shape, monkeypatch
     assert same_rows(st.cpu().numpy(), ref)
 
 
+def wide_step_case(rng, B, N):
+    """A table whose steps break the usual cdf shape: a start of -2^30 and a step of 2^24 - 1, far
+    above 2^fp.  The reference still codes them (a 64-bit renormalisation bound, an exact division),
+    and the states then leave [0, 2^31): rows of wrapped starts followed by the wide step drive
+    the 32-bit states above 2^31 hundreds of times in a 400-symbol row."""
+    base = -(1 << 30)
+    wide = np.array([base, base + 50, base + 50 + (1 << 24) - 1, base + 50 + (1 << 24) + 99,
+                     base + 50 + (1 << 24) + 199], np.int64).astype(np.int32)
+    normal = np.array([0, 1000, 2000, 3000, 4096], np.int32)
+    cdfs = np.stack([wide, normal])
+    sizes = np.full(2, 5, np.int32)
+    offs = np.zeros(2, np.int32)
+    idx = (rng.random((B, N)) < 0.1).astype(np.int32)
+    sym = rng.choice([0, 1, 2, 3], size=(B, N), p=[0.4, 0.4, 0.1, 0.1]).astype(np.int32)
+    return 12, cdfs, sizes, offs, sym, idx
+
+
+@pytest.mark.parametrize("kernel", PUSH_KERNELS)
+@pytest.mark.parametrize("variant", VARIANTS)
+def test_push_steps_wider_than_the_precision(C, kernel, variant, monkeypatch):
+    """Steps wider than 2^fp go through the exact step code of every push kernel (the fast steps'
+    reciprocal quotient holds only below 2^N); rows must equal the oracle's."""
+    monkeypatch.setenv("TORCH_ANS_B200_PUSH_KERNEL", kernel)
+    B, N = 64, 400
+    rng = np.random.default_rng(zlib.crc32(f"wide-{kernel}-{variant}".encode()))
+    fp, cdfs, sizes, offs, sym, idx = wide_step_case(rng, B, N)
+    ref, perr = O.push(variant, O.init_stream(variant, B), sym, idx, cdfs, sizes, offs, fp, False)
+    assert perr == 0
+    st = getattr(C, f"{variant}_init_stream")(B).cuda()
+    getattr(C, f"{variant}_push")(st, t(sym), t(idx), t(cdfs), t(sizes), t(offs), freq_precision=fp,
+                                  bypass_coding=False)
+    assert C.device_status() == 0
+    assert same_rows(st.cpu().numpy(), ref)
+
+
 @pytest.mark.parametrize("streams_per_block,chain_warps,prep_warps",
                          [("1", "1", "1"), ("64", "4", "4"), ("128", "4", "2"), ("37", "8", "8"), ("96", "2", "1")])
 @pytest.mark.parametrize("variant", VARIANTS)

@@ -67,6 +67,14 @@ def _oracle_rows(variant, fp, bypass, lengths, sym, cdfs, sizes, offs, idx=None)
     return pushed, popped, (np.concatenate(dec) if dec else np.zeros(0, np.int32))
 
 
+def _pick_pop(monkeypatch, kernel):
+    """"lean": the lean push chain and pop (where the case allows them), "warp" / "thread": the
+    general push chain with the general warp-per-stream or thread-per-stream pop."""
+    monkeypatch.setenv("TORCH_ANS_B200_RAGGED_POP_WARP", "0" if kernel == "thread" else "1")
+    monkeypatch.setenv("TORCH_ANS_B200_RAGGED_POP_LEAN", "1" if kernel == "lean" else "0")
+    monkeypatch.setenv("TORCH_ANS_B200_RAGGED_PUSH_LEAN", "1" if kernel == "lean" else "0")
+
+
 def _same_row(got_row, want):
     return got_row[0] == want[0, 0] and G.payload_bytes(got_row[None]) == G.payload_bytes(want)
 
@@ -74,12 +82,13 @@ def _same_row(got_row, want):
 @pytest.mark.parametrize("variant", VARIANTS)
 @pytest.mark.parametrize("bypass", [False, True])
 @pytest.mark.parametrize("pattern", ["per_element", "shared_tables"])
-@pytest.mark.parametrize("kernel", ["warp", "thread"])
+@pytest.mark.parametrize("kernel", ["lean", "warp", "thread"])
 def test_ragged_round_trip_matches_per_stream_reference(variant, bypass, pattern, kernel, monkeypatch):
-    """Pops through the warp-per-stream kernel (rows of <= 64 entries) and through the
-    thread-per-stream kernel."""
+    """Pops through the lean warp kernel (consecutive rows of <= 33 entries without bypass coding;
+    other cases fall through to the general one), the general warp-per-stream kernel (rows of <= 64
+    entries) and the thread-per-stream kernel."""
     from torch_ans_b200 import _C
-    monkeypatch.setenv("TORCH_ANS_B200_RAGGED_POP_WARP", "1" if kernel == "warp" else "0")
+    _pick_pop(monkeypatch, kernel)
     rng = np.random.default_rng(zlib.crc32(f"ragged-{variant}-{bypass}-{pattern}".encode()))
     lengths = [0, 1, 3, 4, 5, 17, 64, 257, 1000, 2] + list(rng.integers(0, 400, 30))
     fp, cdfs, sizes, offs, sym = _per_element_case(rng, variant, bypass, lengths)
@@ -151,17 +160,20 @@ def test_ragged_bad_rows_and_indexes_are_flagged(variant):
 
 
 @pytest.mark.parametrize("variant", VARIANTS)
-@pytest.mark.parametrize("case", ["unsorted_rows", "wide_rows", "short_table"])
-def test_ragged_pop_unusual_rows(variant, case):
+@pytest.mark.parametrize("case", ["unsorted_rows", "wide_rows", "short_table", "narrow_rows"])
+@pytest.mark.parametrize("kernel", ["lean", "warp"])
+def test_ragged_pop_unusual_rows(variant, case, kernel, monkeypatch):
     """Rows the ballot search must not take (entries out of order: the reference bisection's
     answer then differs from a count unless the comparison mask is still a prefix, so the kernel
-    runs the bisection itself), rows wider than 64 entries (the thread-per-stream kernel), and a
-    per-element table list shorter than the symbols (the steps past it are bad indexes).  Decoded
-    symbols, rows and error bits must match the oracle's per-stream pops of the same streams."""
+    runs the bisection itself), rows wider than 64 entries (the thread-per-stream kernel), a
+    per-element table list shorter than the symbols (the steps past it are bad indexes) and rows
+    of 21 entries (fewer than the lanes).  Decoded symbols, rows and error bits must match the
+    oracle's per-stream pops of the same streams."""
     from torch_ans_b200 import _C
+    _pick_pop(monkeypatch, kernel)
     rng = np.random.default_rng(zlib.crc32(f"unusual-{variant}-{case}".encode()))
     lengths = [0, 1, 9, 40, 33, 70, 3]
-    A = 100 if case == "wide_rows" else 32
+    A = {"wide_rows": 100, "narrow_rows": 20}.get(case, 32)
     fp, cdfs, sizes, offs, sym = _per_element_case(rng, variant, False, lengths, A=A)
     pushed, _, _ = _oracle_rows(variant, fp, False, lengths, sym, cdfs, sizes, offs)
     pop_cdfs = cdfs.copy()
@@ -198,3 +210,90 @@ def test_ragged_pop_unusual_rows(variant, case):
     got = st.cpu().numpy()
     for b in range(len(lengths)):
         assert _same_row(got[b], rows_ref[b]), f"stream {b}"
+
+
+@pytest.mark.parametrize("variant", VARIANTS)
+@pytest.mark.parametrize("kernel", ["lean", "warp", "thread"])
+def test_ragged_pop_past_the_pushed_words(variant, kernel, monkeypatch):
+    """Each stream pops a few more symbols than were pushed into it: the extra steps read below
+    the first data word (TANS_DEV_UNDERFLOW, zero words, as the oracle's per-stream pops do) and the
+    decoded symbols, the rows left behind (state and length, which goes negative) and the error
+    bits must still equal the oracle's."""
+    from torch_ans_b200 import _C
+    _pick_pop(monkeypatch, kernel)
+    rng = np.random.default_rng(zlib.crc32(f"past-{variant}".encode()))
+    pushed_n = [0, 1, 2, 7, 31, 64, 100, 5]
+    extra = [3, 1, 6, 9, 2, 40, 5, 17]
+    pop_n = [a + e for a, e in zip(pushed_n, extra)]
+    fp, cdfs, sizes, offs, sym = _per_element_case(rng, variant, False, pop_n)
+    starts = np.concatenate([[0], np.cumsum(pop_n)])
+    dec_ref, rows_ref, err_ref = [], [], 0
+    for b, (n, m) in enumerate(zip(pushed_n, pop_n)):
+        lo = int(starts[b])
+        st = O.init_stream(variant, 1)
+        if n:
+            st, e = O.push(variant, st, sym[lo:lo + n][None], np.arange(n, dtype=np.int32)[None],
+                           cdfs[lo:lo + n], sizes[lo:lo + n], offs[lo:lo + n], fp, False)
+            assert e == 0
+        rows_ref.append(st.copy())
+        d, e = O.pop(variant, st, np.arange(m, dtype=np.int32)[None], cdfs[lo:lo + m], sizes[lo:lo + m],
+                     offs[lo:lo + m], fp, False)
+        assert np.array_equal(d.reshape(-1)[:n], sym[lo:lo + n])
+        dec_ref.append(d.reshape(-1))
+        err_ref |= e
+        rows_ref[-1] = (rows_ref[-1], st)
+    assert err_ref & O.ERR_UNDERFLOW
+    Wd = max(r[0].shape[1] for r in rows_ref)
+    host = np.zeros((len(pop_n), Wd), np.int32)
+    for b, (r, _) in enumerate(rows_ref):
+        host[b, : r.shape[1]] = r[0]
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    st = dev(host)
+    dec = getattr(_C, f"{variant}_pop_ragged")(st, torch.from_numpy(starts.astype(np.int64)), dev(cdfs), dev(sizes),
+                                               offsets=dev(offs), freq_precision=fp, bypass_coding=False)
+    assert _C.device_status() == err_ref
+    assert np.array_equal(dec.cpu().numpy(), np.concatenate(dec_ref))
+    got = st.cpu().numpy()
+    head = 3 if variant == "rans64" else 2  # the length word and the state
+    for b, (_, want) in enumerate(rows_ref):
+        assert np.array_equal(got[b][:head], want[0, :head]), f"stream {b}"
+
+
+@pytest.mark.parametrize("variant", VARIANTS)
+@pytest.mark.parametrize("kernel", ["lean", "warp"])
+def test_ragged_push_steps_wider_than_the_precision(variant, kernel, monkeypatch):
+    """Per-element rows with a start of -2^30 and a step of 2^24 - 1 (far above 2^fp): the
+    reference still codes them and its 32-bit states then leave [0, 2^31), where only the exact
+    step code divides correctly.  Rows must equal the oracle's per-stream pushes."""
+    from torch_ans_b200 import _C
+    from tests.test_gpu_parity import wide_step_case
+    _pick_pop(monkeypatch, kernel)
+    rng = np.random.default_rng(zlib.crc32(f"ragged-wide-{variant}".encode()))
+    lengths = [0, 3, 400, 17, 256, 99]
+    fp, tabs, tsizes, toffs, sym2, idx2 = wide_step_case(rng, 1, int(sum(lengths)))
+    sym, k = sym2.reshape(-1), idx2.reshape(-1)
+    cdfs, sizes, offs = tabs[k], tsizes[k], toffs[k]  # one row per symbol
+    pushed, _, _ = _oracle_rows_push_only(variant, fp, lengths, sym, cdfs, sizes, offs)
+    rows = torch.tensor(np.concatenate([[0], np.cumsum(lengths)]), dtype=torch.int64)
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    st = getattr(_C, f"{variant}_init_stream")(len(lengths)).cuda()
+    getattr(_C, f"{variant}_push_ragged")(st, dev(sym), rows.cuda(), dev(cdfs), dev(sizes), offsets=dev(offs),
+                                          freq_precision=fp, bypass_coding=False)
+    assert _C.device_status() == 0
+    got = st.cpu().numpy()
+    for b in range(len(lengths)):
+        assert _same_row(got[b], pushed[b]), f"stream {b} (length {lengths[b]})"
+
+
+def _oracle_rows_push_only(variant, fp, lengths, sym, cdfs, sizes, offs):
+    pushed, lo = [], 0
+    for n in lengths:
+        hi = lo + int(n)
+        st = O.init_stream(variant, 1)
+        if n:
+            st, err = O.push(variant, st, sym[lo:hi][None], np.arange(n, dtype=np.int32)[None], cdfs[lo:hi],
+                             sizes[lo:hi], offs[lo:hi], fp, False)
+            assert err == 0
+        pushed.append(st)
+        lo = hi
+    return pushed, None, None

@@ -78,6 +78,9 @@ template <typename S> __device__ __forceinline__ S to_state(int32_t a) {
 // z = 0 marks an unusable entry (freq <= 0).  Quotient: floor(x / freq) = mulhi(2x, m) >> l for
 // every freq >= 1 and x < 2^N (the GM bound above, with 2x absorbing the one-bit shift; for
 // freq = 1, l = 0 and m = 2^N give floor(2x * 2^N / 2^(N+1)) = x), so there is no special case.
+// The fast steps of the push kernels take only entries with 1 <= freq <= 2^fp: there the
+// renormalised state is below bound = freq << (N - fp) <= 2^N.  Any other step runs push_chain,
+// which divides with quotient_exact.
 __device__ __forceinline__ unsigned ceil_log2(uint32_t d) {  // 0 for d <= 1
   return d > 1u ? 32u - (unsigned)__clz((int)(d - 1u)) : 0u;
 }
@@ -111,6 +114,30 @@ __device__ __forceinline__ typename VT<V>::State quotient(typename VT<V>::State 
   } else {
     return __umulhi(x << 1, e.x) >> l;
   }
+}
+
+// floor(x / freq) for every state x (quotient() needs x < 2^N).  A state of 2^N or more reaches
+// the division only after a step whose frequency exceeds 2^fp (bound = freq << (N - fp) > 2^N):
+// no quantised cdf has one, but the reference divides exactly there too.  With l >= 1,
+// mulhi(x, m) >> (l - 1) = floor(x * m / 2^(N+l)) is floor(x / freq) or one more (m * freq =
+// 2^(N+l) + e with e < freq, so the excess x * e / (freq * 2^(N+l)) is below 2^(1-l) <= 1): one
+// downward correction.  l = 0 is freq = 1.
+template <int V>
+__device__ __forceinline__ typename VT<V>::State quotient_exact(typename VT<V>::State x, uint4 e, bool packed,
+                                                                uint32_t freq) {
+  using S = typename VT<V>::State;
+  const unsigned l = entry_shift(e, packed);
+  if (l == 0u) return x;
+  S q;
+  if constexpr (V == 0) {
+    const unsigned long long m = ((unsigned long long)e.y << 32) | e.x;
+    q = __umul64hi(x, m) >> (l - 1u);
+    if (__umul64hi(q, (unsigned long long)freq) != 0ull || q * (unsigned long long)freq > x) --q;
+  } else {
+    q = __umulhi(x, e.x) >> (l - 1u);
+    if ((unsigned long long)q * freq > (unsigned long long)x) --q;
+  }
+  return q;
 }
 
 // Per-table information, 16 bytes: cdf_size, offset, alias cut width, log2(cut) or -1.

@@ -143,7 +143,7 @@ __device__ __forceinline__ void push_chain(const PushParams& P, typename VT<V>::
 #pragma unroll
   for (int t = 0; t < VT<V>::MAX_RENORM; ++t)
     if ((unsigned long long)x >= bound) c.emit(x);
-  const S q = quotient<V>(x, r.e, packed);
+  const S q = quotient_exact<V>(x, r.e, packed, freq);
   const S start = to_state<S>((int32_t)r.e.w);
   if constexpr (ALIAS) {
     const S ri = (S)(x - q * (S)freq + start);

@@ -109,7 +109,7 @@ __global__ void __launch_bounds__(512) push_fast_kernel(const PushParams P) {
     for (int q = 0; q < 4; ++q) e[q] = ent[(es * 4 + q) * nact + at];
     bool exact = flg[es * nact + at] != 0u;
 #pragma unroll
-    for (int q = 0; q < 4; ++q) exact |= e[q].z == 0u;
+    for (int q = 0; q < 4; ++q) exact |= entry_freq(e[q], true) - 1u >= (1u << P.fp);  // 0 or above 2^fp
     if (exact) {
       // reference-exact steps, last symbol of the chunk first
 #pragma unroll 1

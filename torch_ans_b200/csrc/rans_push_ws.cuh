@@ -171,7 +171,7 @@ __global__ void __launch_bounds__(512) push_ws_kernel(const PushParams P, int sb
           for (int q = 0; q < 4; ++q) e[q] = es[(size_t)(4 * c + q) * sb];
           bool exact = ((fw >> (8 * c)) & 0xFFu) != 0u || !row_ok || p + 4 * MR >= cap;
 #pragma unroll
-          for (int q = 0; q < 4; ++q) exact |= e[q].z == 0u;
+          for (int q = 0; q < 4; ++q) exact |= entry_freq(e[q], true) - 1u >= (1u << P.fp);  // 0 or above 2^fp
           if (exact) {
             const WsState<V> st = pushws_exact_chunk<V, ALIAS, BYPASS>(P, WsState<V>{x, p, err}, b, cr);
             x = st.x;

@@ -55,7 +55,9 @@ __device__ __forceinline__ bool ragged_row(const RaggedArgs& R, int64_t b, int64
 // ---------------------------------------------------------------- push
 // per symbol: the work of push_prepare (rans_utils.hpp:186-215) plus the entry the push builds
 // per table elsewhere (reciprocal of freq, start), from the symbol's own row
-template <int V, bool BYPASS>
+// LEAN (32-bit states, no bypass coding): the flags go into the entry's unused y word and the
+// {escape value, flags} array is not written.
+template <int V, bool BYPASS, bool LEAN = false>
 __global__ void ragged_push_prep_kernel(const RaggedArgs R) {
   uint32_t err = 0;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < R.total; i += (int64_t)gridDim.x * blockDim.x) {
@@ -104,8 +106,13 @@ __global__ void ragged_push_prep_kernel(const RaggedArgs R) {
         a = make_int2(raw, (int)flags);
       }
     }
-    R.ent[i] = e;
-    R.aux[i] = a;
+    if constexpr (LEAN) {
+      e.y = (uint32_t)a.y;
+      R.ent[i] = e;
+    } else {
+      R.ent[i] = e;
+      R.aux[i] = a;
+    }
   }
   report(R.status, err);
 }
@@ -160,7 +167,7 @@ __global__ void __launch_bounds__(256) ragged_push_chain_kernel(const RaggedArgs
     r.rbase = 0;
     r.rcap = 0;
     const uint32_t freq = packed ? entry_freq(r.e, true) : 0u;
-    if (r.flags == 0u && freq != 0u && cur.p >= -1 && cur.p + MR < cur.cap) {
+    if (r.flags == 0u && freq - 1u < (1u << P.fp) && cur.p >= -1 && cur.p + MR < cur.cap) {
       // every word this step can emit lands inside the row: the word goes to the next slot
       // unconditionally and the cursor advances only when it is kept (a slot past the row's final
       // length is never part of its record), so the renormalisation has no branch
@@ -182,6 +189,137 @@ __global__ void __launch_bounds__(256) ragged_push_chain_kernel(const RaggedArgs
   store_state<V>(row, 0, x);
   row[0] = (int32_t)((cur.p + 1) * VT<V>::WBYTES);
   report(R.status, cur.err);
+}
+
+// Lean chain for 32-bit states without bypass coding (prep with LEAN: entry y = flags).  Each
+// thread's entries arrive in a ring of four 16-entry quarters, each filled by one 1D bulk copy
+// (copy engine, completing on the quarter's mbarrier) three quarters ahead of its use; the next
+// step's entry is read from the ring during the current step.  A step whose entry is usable
+// (1 <= freq <= 2^fp) and whose words fit the row takes the fast form: the renormalisation count
+// from MR comparisons made at once ((x >> WB*t) >= bound for t < MR: the reference's loop of
+// rans_utils.hpp:45-49 runs exactly that many times, the conditions being nested), the words
+// stored unconditionally (the cursor advances only over the kept ones), the reciprocal quotient
+// (exact there: the renormalised state is below bound <= 2^31) and C(s, x) of
+// rans_utils.hpp:292.  Any other step runs push_chain, the reference-exact step code.
+constexpr int RQ_ENT = 16;                             // entries per quarter (one bulk copy)
+constexpr int RQ_Q = 4;                                // quarters per thread
+constexpr int RQ_STRIDE = RQ_Q * RQ_ENT * 16 + 16;     // ring bytes per thread (+16: threads on distinct banks)
+constexpr int RQ_SMEM = RQ_STRIDE + RQ_Q * 8;          // + one mbarrier per quarter
+constexpr unsigned RQ_WAIT_LIMIT = 1u << 20;           // tries of a copy-completion wait
+
+template <int V>
+__global__ void __launch_bounds__(256) ragged_push_lean_kernel(const RaggedArgs R, const PushParams P) {
+  static_assert(V == 1 || V == 2, "32-bit states only");
+  using W = typename VT<V>::Word;
+  constexpr int MR = VT<V>::MAX_RENORM;
+  constexpr int WB = VT<V>::WB;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  const int T = blockDim.x, tid = threadIdx.x;
+  uint4* ring = reinterpret_cast<uint4*>(smem_raw + (size_t)tid * RQ_STRIDE);
+  unsigned long long* bar = reinterpret_cast<unsigned long long*>(smem_raw + (size_t)T * RQ_STRIDE) + tid * RQ_Q;
+  const int64_t b = (int64_t)blockIdx.x * T + tid;
+  if (b >= R.batch) return;
+  int64_t lo, hi;
+  if (!ragged_row(R, b, lo, hi)) {
+    report(R.status, DEV_BAD_VALUE);
+    return;
+  }
+  int32_t* row = R.stream + b * R.width;
+  uint8_t* payload = reinterpret_cast<uint8_t*>(row + 1);
+  W* words = reinterpret_cast<W*>(payload);
+  int64_t p = (int64_t)row[0] / VT<V>::WBYTES - 1;  // last written word
+  const int64_t cap = (R.width - 1) * 4 / VT<V>::WBYTES;
+  // fast steps need p >= -1 (a length outside the row sends every step the exact way) and room for
+  // MR words after p
+  const int64_t pfast = p >= -1 ? cap - MR : INT64_MIN;
+  uint32_t x = (uint32_t)load_state<V>(row, 0);
+  uint32_t err = 0;
+  const int fp = P.fp;
+  const int shift = VT<V>::USED - fp;
+  const uint32_t one = 1u << fp;
+  const int64_t n = hi - lo;
+  const int64_t nch = (n + RQ_ENT - 1) / RQ_ENT;
+  // quarter c & 3 <- the entries of steps [16c, 16c + 16), last step first in memory order, so
+  // step 16c + j reads slot 15 - j
+  auto issue = [&](int64_t c) {
+    const int cnt = (int)min((int64_t)RQ_ENT, n - c * RQ_ENT);
+    const int q = (int)(c & (RQ_Q - 1));
+    mbar_arrive_expect_tx(bar + q, (unsigned)cnt * 16u);
+    bulk_copy_g2s(ring + q * RQ_ENT + (RQ_ENT - cnt), R.ent + (hi - c * RQ_ENT - cnt), (unsigned)cnt * 16u, bar + q);
+  };
+  auto wait = [&](int64_t c) -> bool {
+    const int q = (int)(c & (RQ_Q - 1));
+    const unsigned par = (unsigned)((c >> 2) & 1);
+    for (unsigned it = 0; it < RQ_WAIT_LIMIT; ++it)
+      if (mbar_try_wait(bar + q, par)) return true;
+    return false;
+  };
+  if (nch > 0) {
+    for (int q = 0; q < RQ_Q; ++q) mbar_init(bar + q, 1u);
+    mbar_init_fence();
+    for (int64_t c = 0; c < min(nch, (int64_t)RQ_Q); ++c) issue(c);
+  }
+  int64_t c = 0;
+  for (; c < nch; ++c) {
+    if (!wait(c)) {
+      err |= DEV_STALLED;
+      break;
+    }
+    const int cnt = (int)min((int64_t)RQ_ENT, n - c * RQ_ENT);
+    const uint4* ch = ring + (c & (RQ_Q - 1)) * RQ_ENT + (RQ_ENT - 1);
+    uint4 e = ch[0];
+#pragma unroll 1
+    for (int j = 0; j < cnt; ++j) {
+      const uint4 en = j + 1 < cnt ? ch[-(j + 1)] : e;
+      const uint32_t freq = e.z & 0xFFFFFFu;
+      if (e.y == 0u && freq - 1u < one && p < pfast) {
+        const uint32_t bound = freq << shift;
+        W* wp = words + (p + 1);
+        int k;
+        if constexpr (V == 1) {
+          const uint32_t x8 = x >> 8, x16 = x >> 16;
+          k = (x >= bound ? 1 : 0) + (x8 >= bound ? 1 : 0) + (x16 >= bound ? 1 : 0);
+          wp[0] = (W)x;
+          wp[1] = (W)x8;
+          wp[2] = (W)x16;
+        } else {
+          k = x >= bound ? 1 : 0;
+          wp[0] = (W)x;
+        }
+        x >>= WB * k;
+        p += k;
+        const uint32_t qt = __umulhi(x << 1, e.x) >> (e.z >> 24);
+        x = x + e.w + qt * (one - freq);
+      } else {
+        PushCursor<V> cur;
+        cur.payload = payload;
+        cur.p = p;
+        cur.cap = cap;
+        cur.err = err;
+        PushPrep r;
+        r.e = e;
+        r.flags = e.y;
+        r.raw = 0;
+        r.rbase = 0;
+        r.rcap = 0;
+        typename VT<V>::State xs = x;
+        push_chain<V, false, false>(P, xs, cur, r);
+        x = (uint32_t)xs;
+        p = cur.p;
+        err = cur.err;
+      }
+      e = en;
+    }
+    if (c + RQ_Q < nch) {
+      fence_proxy_async_shared();  // this thread's reads of the quarter come before the copy's writes
+      issue(c + RQ_Q);
+    }
+  }
+  // a wait that gave up leaves copies in flight: wait (bounded) for them before leaving
+  for (int64_t d = c; d < min(nch, c + RQ_Q); ++d) wait(d);
+  store_state<V>(row, 0, (typename VT<V>::State)x);
+  row[0] = (int32_t)((p + 1) * VT<V>::WBYTES);
+  report(R.status, err);
 }
 
 // ---------------------------------------------------------------- pop
@@ -532,6 +670,180 @@ __global__ void __launch_bounds__(256) ragged_pop_warp_kernel(const RaggedArgs R
   }
 }
 
+// Lean warp pop for the common per-element case: consecutive rows (no table indexes) of at most 33
+// entries, no bypass coding.  Same results as ragged_pop_warp_kernel; the step is rebuilt around a
+// short dependent chain:
+//   * lane l compares entry l + 1 (l + 1 < size) with cum, so s = popc(ballot) directly, and every
+//     lane forms the candidate state (x >> fp) * (row[l+1] - row[l]) + cum - row[l] beside the
+//     vote; one shuffle from lane s gives D(x) (rans_utils.hpp:466-471).  The exactness test of
+//     ragged_pop_warp_kernel (entry 0 <= cum, the mask a prefix, entry size - 1 > cum) gates it;
+//     any other row takes the reference bisection on the staged row.
+//   * the words ahead of the cursor sit in a 64-bit register window (refilled one aligned 32-bit
+//     unit at a time, the next unit already loaded), so the renormalisation of
+//     rans_utils.hpp:473-475 is one count of the words needed and one funnel shift.
+//   * the next step's row entries are read from shared memory during the current step, and 16
+//     rows are staged per copy round so that every warp of a 4,096-stream call is resident at once.
+constexpr int RL_ROWS = 16;  // rows per staging buffer
+
+__host__ __device__ inline size_t ragged_lean_words(int64_t cdf_width) {
+  return 2 * (RL_ROWS * (size_t)cdf_width + 2 * RL_ROWS);
+}
+
+template <int V>
+__global__ void __launch_bounds__(256, 4) ragged_pop_lean_kernel(const RaggedArgs R, const PopParams P) {
+  using S = typename VT<V>::State;
+  constexpr int WB = VT<V>::WB;
+  constexpr int WPU = 32 / WB;                 // words per 32-bit unit
+  constexpr int LWPU = WPU == 4 ? 2 : (WPU == 2 ? 1 : 0);
+  constexpr int MR = VT<V>::MAX_RENORM;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  const int warps = blockDim.x >> 5, wib = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int W = (int)R.cdf_width;
+  int32_t* ring = reinterpret_cast<int32_t*>(smem_raw) + (size_t)wib * ragged_lean_words(W);
+  const int64_t b = (int64_t)blockIdx.x * warps + wib;
+  if (b >= R.batch) return;
+  int64_t lo, hi;
+  if (!ragged_row(R, b, lo, hi) || hi - lo > 0x7fffff00) {
+    if (lane == 0) report(R.status, DEV_BAD_VALUE);
+    return;
+  }
+  int32_t* row = R.stream + b * R.width;
+  const uint32_t* pu = reinterpret_cast<const uint32_t*>(row + 1);
+  const int first = VT<V>::SBYTES / VT<V>::WBYTES;       // words below hold the state
+  const int ufirst = VT<V>::SBYTES / 4;
+  const int64_t capw64 = (R.width - 1) * 4 / VT<V>::WBYTES;
+  const int capw = (int)min(capw64, (int64_t)0x7fffffff);
+  const int capu = (int)min(R.width - 1, (int64_t)0x7fffffff);
+  // a word outside [first, capw) reads as 0, as the reference-order cursor of the other pops does
+  auto unit = [&](int q) -> uint32_t { return (q >= ufirst && q < capu) ? __ldg(pu + q) : 0u; };
+  const int64_t p64 = (int64_t)row[0] / VT<V>::WBYTES - 1;
+  int p = (int)min(max(p64, (int64_t)-0x7fffffff), (int64_t)0x7fffffff);  // next word to read
+  // window: the next words to read, the first in the top bits; nbits > 32 before every step
+  int q = p >> LWPU;
+  uint64_t win = (uint64_t)(unit(q) << (WB * (WPU - 1 - (p & (WPU - 1))))) << 32;
+  int nbits = WB * ((p & (WPU - 1)) + 1);
+  win |= (uint64_t)unit(q - 1) << (32 - nbits);
+  nbits += 32;
+  q -= 2;
+  uint32_t nu = unit(q);
+  uint32_t err = 0;
+  S x = load_state<V>(row, 0);
+  const int n = (int)(hi - lo);
+  const uint32_t cmask = (1u << R.fp) - 1u;
+  const int fp = R.fp;
+  const int bstride = RL_ROWS * W + 2 * RL_ROWS;
+  const int nblk = (n + RL_ROWS - 1) / RL_ROWS;
+  // rows [t0, t0 + 16) of the stream with their sizes and offsets into one buffer
+  auto stage = [&](int blk) {
+    int32_t* buf = ring + (blk & 1) * bstride;
+    const int64_t t0 = lo + (int64_t)blk * RL_ROWS;
+    const int nr = min(RL_ROWS, n - blk * RL_ROWS);
+    const int vr = (int)max((int64_t)0, min((int64_t)nr, R.ntables - t0));
+    const int32_t* src = R.cdfs + t0 * R.cdf_width;
+    for (int i = lane; i < vr * W; i += 32) cp_async4(buf + i, src + i);
+    if (lane < vr) {
+      cp_async4(buf + RL_ROWS * W + lane, R.sizes + t0 + lane);
+      if (R.offsets) cp_async4(buf + RL_ROWS * W + RL_ROWS + lane, R.offsets + t0 + lane);
+    }
+  };
+  if (nblk > 0) stage(0);
+  cp_async_commit();
+  for (int blk = 0; blk < nblk; ++blk) {
+    if (blk + 1 < nblk) stage(blk + 1);
+    cp_async_commit();
+    cp_async_wait<1>();
+    __syncwarp();  // every lane's staged words are visible to the whole warp
+    const int32_t* buf = ring + (blk & 1) * bstride;
+    const int t0 = blk * RL_ROWS;
+    const int nr = min(RL_ROWS, n - t0);
+    const int vr = (int)max((int64_t)0, min((int64_t)nr, R.ntables - (lo + t0)));
+    // lane l < nr: the offset of this block's row l (its decoded symbol leaves from lane l)
+    const int32_t myoff = (R.offsets && lane < vr) ? buf[RL_ROWS * W + RL_ROWS + lane] : 0;
+    int32_t outv = 0;
+    // entries of the step about to run: row[l], row[l + 1], row[0], size
+    int32_t c0 = 0, c1 = 0, r0 = 0, size = 0;
+    if (vr > 0) {
+      c0 = buf[lane];
+      c1 = buf[lane + 1];
+      r0 = buf[0];
+      size = buf[RL_ROWS * W];
+    }
+#pragma unroll 1
+    for (int r = 0; r < vr; ++r) {
+      const int32_t* slot = buf + r * W;
+      int32_t c0n = 0, c1n = 0, r0n = 0, sizen = 0;
+      if (r + 1 < vr) {  // the next step's entries, off the chain
+        c0n = slot[W + lane];
+        c1n = slot[W + lane + 1];
+        r0n = slot[W];
+        sizen = buf[RL_ROWS * W + r + 1];
+      }
+      const int32_t c1m = lane + 1 < size ? c1 : 0x7fffffff;
+      const int32_t cum = (int32_t)((uint32_t)x & cmask);
+      const unsigned m = __ballot_sync(0xffffffffu, c1m <= cum);
+      const int s = __popc(m);
+      const S cand = (S)((x >> fp) * to_state<S>((int32_t)((uint32_t)c1 - (uint32_t)c0)) +
+                         to_state<S>((int32_t)((uint32_t)cum - (uint32_t)c0)));
+      S xn = __shfl_sync(0xffffffffu, cand, s & 31);
+      const bool fast = size >= 2 && size <= W && cum >= r0 && (m & (m + 1u)) == 0u && ((m >> ((size - 2) & 31)) & 1u) == 0u;
+      int32_t sym = s;
+      bool ok = true;
+      if (!fast) {  // any other row: the reference bisection on the staged row
+        TableInfo tinf;
+        tinf.size = size;
+        tinf.offset = 0;
+        tinf.cut = 0;
+        tinf.cut_log2 = -1;
+        int64_t s64;
+        int32_t cum_off, freq;
+        ok = lookup_symbol<V, LK_SEARCH, false>(slot, tinf, cum, R.cdf_width, fp, s64, cum_off, freq);
+        if (ok) {
+          xn = (S)((x >> fp) * to_state<S>(freq) + to_state<S>(cum_off));
+          sym = (int32_t)s64;
+        } else {
+          err |= DEV_BAD_VALUE;
+        }
+      }
+      if (ok) {
+        // words needed: the reference's renormalisation loop count (at most MR)
+        int k = 0;
+#pragma unroll
+        for (int t = 0; t < MR; ++t) k += (unsigned long long)xn < (VT<V>::LB >> (WB * t)) ? 1 : 0;
+        const int bits = WB * k;
+        const uint32_t top = (uint32_t)(win >> 32);
+        if constexpr (V == 0) {
+          x = bits ? (S)((xn << 32) | top) : xn;
+        } else {
+          x = __funnelshift_lc(top, xn, bits);
+        }
+        if (k > 0 && (p >= capw || p < first + k - 1)) err |= DEV_UNDERFLOW;
+        p = (int)((unsigned)p - (unsigned)k);
+        win <<= bits;
+        nbits -= bits;
+        if (nbits <= 32) {
+          win |= (uint64_t)nu << (32 - nbits);
+          nbits += 32;
+          nu = unit(--q);
+        }
+      }
+      if (lane == r) outv = ok ? (int32_t)((uint32_t)sym + (uint32_t)myoff) : 0;
+      c0 = c0n;
+      c1 = c1n;
+      r0 = r0n;
+      size = sizen;
+    }
+    if (vr < nr) err |= DEV_BAD_INDEX;  // rows past the table list decode as 0
+    if (lane < nr) R.out[lo + t0 + lane] = outv;
+    __syncwarp();  // the buffer is restaged only after every lane has read it
+  }
+  cp_async_wait<0>();
+  if (lane == 0) {
+    store_state<V>(row, 0, x);
+    row[0] = (int32_t)((int64_t)(p + 1) * VT<V>::WBYTES);
+    report(R.status, err);
+  }
+}
+
 // ---------------------------------------------------------------- host side
 static int ragged_threads(int64_t batch, int sms, int64_t smem_per_thread, int max_threads) {
   int64_t t = (batch + sms - 1) / sms;
@@ -544,6 +856,24 @@ static int ragged_threads(int64_t batch, int sms, int64_t smem_per_thread, int m
 template <int V, bool BY>
 static void ragged_push_launch(const RaggedArgs& R, const PushParams& P, int sms, cudaStream_t s) {
   const int pb = (int)std::max<int64_t>(1, std::min<int64_t>((R.total + 255) / 256, 16 * (int64_t)sms));
+  if constexpr (V != 0 && !BY) {
+    // the entry array must be 16-byte aligned for the bulk copies (the library's own workspace
+    // and any aligned caller buffer are)
+    if (R.fp <= 23 && (reinterpret_cast<uintptr_t>(R.ent) & 15u) == 0 &&
+        env_int("TORCH_ANS_B200_RAGGED_PUSH_LEAN", 1) != 0) {
+      if (R.total > 0) {
+        ragged_push_prep_kernel<V, false, true><<<pb, 256, 0, s>>>(R);
+        note_launch();
+      }
+      const int T = ragged_threads(R.batch, sms, RQ_SMEM, 256);
+      const size_t smem = (size_t)T * RQ_SMEM;
+      if (smem > 48 * 1024)
+        cudaFuncSetAttribute(ragged_push_lean_kernel<V>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      ragged_push_lean_kernel<V><<<(int)((R.batch + T - 1) / T), T, smem, s>>>(R, P);
+      note_launch();
+      return;
+    }
+  }
   if (R.total > 0) {
     ragged_push_prep_kernel<V, BY><<<pb, 256, 0, s>>>(R);
     note_launch();
@@ -569,10 +899,27 @@ static void ragged_pop_warp_go(const RaggedArgs& R, const PopParams& P, int sms,
   note_launch();
 }
 
+template <int V>
+static void ragged_pop_lean_go(const RaggedArgs& R, const PopParams& P, int sms, cudaStream_t s) {
+  int64_t warps = (R.batch + sms - 1) / sms;
+  warps = std::max<int64_t>(1, std::min<int64_t>(warps, 8));
+  const size_t smem = (size_t)warps * ragged_lean_words(R.cdf_width) * sizeof(int32_t);
+  if (smem > 48 * 1024)
+    cudaFuncSetAttribute(ragged_pop_lean_kernel<V>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  ragged_pop_lean_kernel<V><<<(int)((R.batch + warps - 1) / warps), (int)(warps * 32), smem, s>>>(R, P);
+  note_launch();
+}
+
 // without table indexes the rows of consecutive symbols are consecutive: block staging
 template <int V, bool BY>
 static void ragged_pop_warp_launch(const RaggedArgs& R, const PopParams& P, int sms, cudaStream_t s) {
   const bool contig = R.idx == nullptr;
+  if constexpr (!BY) {
+    if (contig && R.cdf_width <= 33 && env_int("TORCH_ANS_B200_RAGGED_POP_LEAN", 1) != 0) {
+      ragged_pop_lean_go<V>(R, P, sms, s);
+      return;
+    }
+  }
   if (R.cdf_width <= 33) {
     if (contig) ragged_pop_warp_go<V, BY, false, true>(R, P, sms, s);
     else ragged_pop_warp_go<V, BY, false, false>(R, P, sms, s);
