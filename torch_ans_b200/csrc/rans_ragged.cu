@@ -55,8 +55,10 @@ __device__ __forceinline__ bool ragged_row(const RaggedArgs& R, int64_t b, int64
 // ---------------------------------------------------------------- push
 // per symbol: the work of push_prepare (rans_utils.hpp:186-215) plus the entry the push builds
 // per table elsewhere (reciprocal of freq, start), from the symbol's own row
-// LEAN (32-bit states, no bypass coding): the flags go into the entry's unused y word and the
-// {escape value, flags} array is not written.
+// LEAN (32-bit states, no bypass coding): the chain's own entry {reciprocal m, (2^fp - freq) |
+// (l - 1) << 24, bound = freq << (31 - fp), start}, with bit 31 of y set (and the rest unused) when
+// the step must take the exact code (flags, freq < 2 or freq > 2^fp); the second array then keeps
+// {the standard entry's z word, flags} for that code.
 template <int V, bool BYPASS, bool LEAN = false>
 __global__ void ragged_push_prep_kernel(const RaggedArgs R) {
   uint32_t err = 0;
@@ -107,8 +109,15 @@ __global__ void ragged_push_prep_kernel(const RaggedArgs R) {
       }
     }
     if constexpr (LEAN) {
-      e.y = (uint32_t)a.y;
-      R.ent[i] = e;
+      const uint32_t freq = e.z & 0xFFFFFFu, l = e.z >> 24;
+      const bool fast = a.y == 0 && freq >= 2u && freq <= (1u << R.fp);
+      uint4 le;
+      le.x = e.x;
+      le.y = fast ? (((1u << R.fp) - freq) | ((l - 1u) << 24)) : 0x80000000u;
+      le.z = fast ? freq << (VT<V>::USED - R.fp) : 0u;
+      le.w = e.w;
+      R.ent[i] = le;
+      R.aux[i] = make_int2((int)e.z, a.y);
     } else {
       R.ent[i] = e;
       R.aux[i] = a;
@@ -191,16 +200,17 @@ __global__ void __launch_bounds__(256) ragged_push_chain_kernel(const RaggedArgs
   report(R.status, cur.err);
 }
 
-// Lean chain for 32-bit states without bypass coding (prep with LEAN: entry y = flags).  Each
+// Lean chain for 32-bit states without bypass coding (entries from the LEAN prep).  Each
 // thread's entries arrive in a ring of four 16-entry quarters, each filled by one 1D bulk copy
 // (copy engine, completing on the quarter's mbarrier) three quarters ahead of its use; the next
 // step's entry is read from the ring during the current step.  A step whose entry is usable
-// (1 <= freq <= 2^fp) and whose words fit the row takes the fast form: the renormalisation count
+// (2 <= freq <= 2^fp) and whose words fit the row takes the fast form: the renormalisation count
 // from MR comparisons made at once ((x >> WB*t) >= bound for t < MR: the reference's loop of
 // rans_utils.hpp:45-49 runs exactly that many times, the conditions being nested), the words
 // stored unconditionally (the cursor advances only over the kept ones), the reciprocal quotient
-// (exact there: the renormalised state is below bound <= 2^31) and C(s, x) of
-// rans_utils.hpp:292.  Any other step runs push_chain, the reference-exact step code.
+// mulhi(x, m) >> (l - 1) = floor(x * m / 2^(31+l)) (exact there: the renormalised state is below
+// bound <= 2^31) and C(s, x) of rans_utils.hpp:292.  Any other step runs push_chain, the
+// reference-exact step code, on the standard entry rebuilt from the second array.
 constexpr int RQ_ENT = 16;                             // entries per quarter (one bulk copy)
 constexpr int RQ_Q = 4;                                // quarters per thread
 constexpr int RQ_STRIDE = RQ_Q * RQ_ENT * 16 + 16;     // ring bytes per thread (+16: threads on distinct banks)
@@ -234,9 +244,6 @@ __global__ void __launch_bounds__(256) ragged_push_lean_kernel(const RaggedArgs 
   const int64_t pfast = p >= -1 ? cap - MR : INT64_MIN;
   uint32_t x = (uint32_t)load_state<V>(row, 0);
   uint32_t err = 0;
-  const int fp = P.fp;
-  const int shift = VT<V>::USED - fp;
-  const uint32_t one = 1u << fp;
   const int64_t n = hi - lo;
   const int64_t nch = (n + RQ_ENT - 1) / RQ_ENT;
   // quarter c & 3 <- the entries of steps [16c, 16c + 16), last step first in memory order, so
@@ -271,9 +278,8 @@ __global__ void __launch_bounds__(256) ragged_push_lean_kernel(const RaggedArgs 
 #pragma unroll 1
     for (int j = 0; j < cnt; ++j) {
       const uint4 en = j + 1 < cnt ? ch[-(j + 1)] : e;
-      const uint32_t freq = e.z & 0xFFFFFFu;
-      if (e.y == 0u && freq - 1u < one && p < pfast) {
-        const uint32_t bound = freq << shift;
+      if ((int32_t)e.y >= 0 && p < pfast) {
+        const uint32_t bound = e.z;
         W* wp = words + (p + 1);
         int k;
         if constexpr (V == 1) {
@@ -288,17 +294,18 @@ __global__ void __launch_bounds__(256) ragged_push_lean_kernel(const RaggedArgs 
         }
         x >>= WB * k;
         p += k;
-        const uint32_t qt = __umulhi(x << 1, e.x) >> (e.z >> 24);
-        x = x + e.w + qt * (one - freq);
+        const uint32_t qt = __umulhi(x, e.x) >> (e.y >> 24);
+        x = x + e.w + qt * (e.y & 0xFFFFFFu);
       } else {
+        const int2 a = R.aux[hi - 1 - (c * RQ_ENT + j)];
         PushCursor<V> cur;
         cur.payload = payload;
         cur.p = p;
         cur.cap = cap;
         cur.err = err;
         PushPrep r;
-        r.e = e;
-        r.flags = e.y;
+        r.e = make_uint4(e.x, 0u, (uint32_t)a.x, e.w);
+        r.flags = (uint32_t)a.y;
         r.raw = 0;
         r.rbase = 0;
         r.rcap = 0;
@@ -675,14 +682,18 @@ __global__ void __launch_bounds__(256) ragged_pop_warp_kernel(const RaggedArgs R
 // short dependent chain:
 //   * lane l compares entry l + 1 (l + 1 < size) with cum, so s = popc(ballot) directly, and every
 //     lane forms the candidate state (x >> fp) * (row[l+1] - row[l]) + cum - row[l] beside the
-//     vote; one shuffle from lane s gives D(x) (rans_utils.hpp:466-471).  The exactness test of
-//     ragged_pop_warp_kernel (entry 0 <= cum, the mask a prefix, entry size - 1 > cum) gates it;
-//     any other row takes the reference bisection on the staged row.
-//   * the words ahead of the cursor sit in a 64-bit register window (refilled one aligned 32-bit
-//     unit at a time, the next unit already loaded), so the renormalisation of
-//     rans_utils.hpp:473-475 is one count of the words needed and one funnel shift.
-//   * the next step's row entries are read from shared memory during the current step, and 16
-//     rows are staged per copy round so that every warp of a 4,096-stream call is resident at once.
+//     vote; one shuffle from lane s gives D(x) (rans_utils.hpp:466-471).
+//   * the exactness test of ragged_pop_warp_kernel in three comparisons: the mask is a prefix
+//     (m & (m + 1) == 0, so m = 2^s - 1), entry size - 1 is above cum (s <= size - 2, with a
+//     usable size folded into the bound) and entry 0 is not.  Then the reference bisection
+//     (rans_utils.hpp:424-450) ends at s; any other step runs that bisection on the staged row.
+//   * the words ahead of the cursor sit in a 64-bit register window (two 32-bit halves moved by
+//     funnel shifts, refilled one aligned 32-bit unit at a time, the next unit already loaded), so
+//     the renormalisation of rans_utils.hpp:473-475 is a count of the words needed and a funnel
+//     shift.
+//   * the next step's row entries are read from shared memory during the current step (without a
+//     branch: the last step of a block reads a row it does not use), and 16 rows are staged per
+//     copy round so that every warp of a 4,096-stream call is resident at once.
 constexpr int RL_ROWS = 16;  // rows per staging buffer
 
 __host__ __device__ inline size_t ragged_lean_words(int64_t cdf_width) {
@@ -693,7 +704,7 @@ template <int V>
 __global__ void __launch_bounds__(256, 4) ragged_pop_lean_kernel(const RaggedArgs R, const PopParams P) {
   using S = typename VT<V>::State;
   constexpr int WB = VT<V>::WB;
-  constexpr int WPU = 32 / WB;                 // words per 32-bit unit
+  constexpr int WPU = 32 / WB;  // words per 32-bit unit
   constexpr int LWPU = WPU == 4 ? 2 : (WPU == 2 ? 1 : 0);
   constexpr int MR = VT<V>::MAX_RENORM;
   extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -709,20 +720,22 @@ __global__ void __launch_bounds__(256, 4) ragged_pop_lean_kernel(const RaggedArg
   }
   int32_t* row = R.stream + b * R.width;
   const uint32_t* pu = reinterpret_cast<const uint32_t*>(row + 1);
-  const int first = VT<V>::SBYTES / VT<V>::WBYTES;       // words below hold the state
+  const int first = VT<V>::SBYTES / VT<V>::WBYTES;  // words below hold the state
   const int ufirst = VT<V>::SBYTES / 4;
-  const int64_t capw64 = (R.width - 1) * 4 / VT<V>::WBYTES;
-  const int capw = (int)min(capw64, (int64_t)0x7fffffff);
+  const int capw = (int)min((R.width - 1) * 4 / VT<V>::WBYTES, (int64_t)0x7fffffff);
   const int capu = (int)min(R.width - 1, (int64_t)0x7fffffff);
   // a word outside [first, capw) reads as 0, as the reference-order cursor of the other pops does
-  auto unit = [&](int q) -> uint32_t { return (q >= ufirst && q < capu) ? __ldg(pu + q) : 0u; };
+  auto unit = [&](int u) -> uint32_t { return (u >= ufirst && u < capu) ? __ldg(pu + u) : 0u; };
   const int64_t p64 = (int64_t)row[0] / VT<V>::WBYTES - 1;
   int p = (int)min(max(p64, (int64_t)-0x7fffffff), (int64_t)0x7fffffff);  // next word to read
-  // window: the next words to read, the first in the top bits; nbits > 32 before every step
+  // window wh:wl: the next words to read, the first in the top bits of wh, nbits of them (> 32
+  // before every step); nu = unit q, merged when nbits drops to 32 or below
   int q = p >> LWPU;
-  uint64_t win = (uint64_t)(unit(q) << (WB * (WPU - 1 - (p & (WPU - 1))))) << 32;
+  uint32_t wh = unit(q) << (WB * (WPU - 1 - (p & (WPU - 1))));
   int nbits = WB * ((p & (WPU - 1)) + 1);
-  win |= (uint64_t)unit(q - 1) << (32 - nbits);
+  const uint32_t u1 = unit(q - 1);
+  wh |= __funnelshift_rc(u1, 0u, nbits);  // u1 >> nbits (nothing for nbits = 32)
+  uint32_t wl = u1 << (32 - nbits);
   nbits += 32;
   q -= 2;
   uint32_t nu = unit(q);
@@ -757,27 +770,19 @@ __global__ void __launch_bounds__(256, 4) ragged_pop_lean_kernel(const RaggedArg
     const int t0 = blk * RL_ROWS;
     const int nr = min(RL_ROWS, n - t0);
     const int vr = (int)max((int64_t)0, min((int64_t)nr, R.ntables - (lo + t0)));
-    // lane l < nr: the offset of this block's row l (its decoded symbol leaves from lane l)
+    // lane l < vr: the offset of this block's row l (its decoded symbol leaves from lane l)
     const int32_t myoff = (R.offsets && lane < vr) ? buf[RL_ROWS * W + RL_ROWS + lane] : 0;
     int32_t outv = 0;
-    // entries of the step about to run: row[l], row[l + 1], row[0], size
-    int32_t c0 = 0, c1 = 0, r0 = 0, size = 0;
-    if (vr > 0) {
-      c0 = buf[lane];
-      c1 = buf[lane + 1];
-      r0 = buf[0];
-      size = buf[RL_ROWS * W];
-    }
+    // the step's row: entries l and l + 1 of this lane, entry 0, size
+    int32_t c0 = buf[lane], c1 = buf[lane + 1], r0 = buf[0];
+    int32_t size = buf[RL_ROWS * W];
 #pragma unroll 1
     for (int r = 0; r < vr; ++r) {
-      const int32_t* slot = buf + r * W;
-      int32_t c0n = 0, c1n = 0, r0n = 0, sizen = 0;
-      if (r + 1 < vr) {  // the next step's entries, off the chain
-        c0n = slot[W + lane];
-        c1n = slot[W + lane + 1];
-        r0n = slot[W];
-        sizen = buf[RL_ROWS * W + r + 1];
-      }
+      const int rn = min(r + 1, RL_ROWS - 1);  // the next step's row, read off the chain
+      const int32_t* sn = buf + rn * W;
+      const int32_t c0n = sn[lane], c1n = sn[lane + 1], r0n = sn[0];
+      const int32_t sizen = buf[RL_ROWS * W + rn];
+      const int32_t lim = (size >= 2 && size <= W) ? size - 2 : -1;
       const int32_t c1m = lane + 1 < size ? c1 : 0x7fffffff;
       const int32_t cum = (int32_t)((uint32_t)x & cmask);
       const unsigned m = __ballot_sync(0xffffffffu, c1m <= cum);
@@ -785,10 +790,9 @@ __global__ void __launch_bounds__(256, 4) ragged_pop_lean_kernel(const RaggedArg
       const S cand = (S)((x >> fp) * to_state<S>((int32_t)((uint32_t)c1 - (uint32_t)c0)) +
                          to_state<S>((int32_t)((uint32_t)cum - (uint32_t)c0)));
       S xn = __shfl_sync(0xffffffffu, cand, s & 31);
-      const bool fast = size >= 2 && size <= W && cum >= r0 && (m & (m + 1u)) == 0u && ((m >> ((size - 2) & 31)) & 1u) == 0u;
       int32_t sym = s;
       bool ok = true;
-      if (!fast) {  // any other row: the reference bisection on the staged row
+      if (!((m & (m + 1u)) == 0u && s <= lim && cum >= r0)) {
         TableInfo tinf;
         tinf.size = size;
         tinf.offset = 0;
@@ -796,37 +800,40 @@ __global__ void __launch_bounds__(256, 4) ragged_pop_lean_kernel(const RaggedArg
         tinf.cut_log2 = -1;
         int64_t s64;
         int32_t cum_off, freq;
-        ok = lookup_symbol<V, LK_SEARCH, false>(slot, tinf, cum, R.cdf_width, fp, s64, cum_off, freq);
+        ok = lookup_symbol<V, LK_SEARCH, false>(buf + r * W, tinf, cum, R.cdf_width, fp, s64, cum_off, freq);
         if (ok) {
           xn = (S)((x >> fp) * to_state<S>(freq) + to_state<S>(cum_off));
           sym = (int32_t)s64;
         } else {
-          err |= DEV_BAD_VALUE;
+          err |= DEV_BAD_VALUE;  // the state stays, the step decodes 0
         }
       }
       if (ok) {
         // words needed: the reference's renormalisation loop count (at most MR)
         int k = 0;
 #pragma unroll
-        for (int t = 0; t < MR; ++t) k += (unsigned long long)xn < (VT<V>::LB >> (WB * t)) ? 1 : 0;
+        for (int t = 0; t < MR; ++t) k += (xn < (S)(VT<V>::LB >> (WB * t))) ? 1 : 0;
         const int bits = WB * k;
-        const uint32_t top = (uint32_t)(win >> 32);
         if constexpr (V == 0) {
-          x = bits ? (S)((xn << 32) | top) : xn;
+          x = bits ? (S)((xn << 32) | wh) : xn;
+          wh = bits ? wl : wh;
+          wl = bits ? 0u : wl;
         } else {
-          x = __funnelshift_lc(top, xn, bits);
+          x = __funnelshift_lc(wh, xn, bits);
+          wh = __funnelshift_l(wl, wh, bits);
+          wl <<= bits;
         }
         if (k > 0 && (p >= capw || p < first + k - 1)) err |= DEV_UNDERFLOW;
         p = (int)((unsigned)p - (unsigned)k);
-        win <<= bits;
         nbits -= bits;
         if (nbits <= 32) {
-          win |= (uint64_t)nu << (32 - nbits);
+          wh |= __funnelshift_rc(nu, 0u, nbits);
+          wl = nu << ((32 - nbits) & 31);
           nbits += 32;
           nu = unit(--q);
         }
       }
-      if (lane == r) outv = ok ? (int32_t)((uint32_t)sym + (uint32_t)myoff) : 0;
+      outv = lane == r ? (ok ? (int32_t)((uint32_t)sym + (uint32_t)myoff) : 0) : outv;
       c0 = c0n;
       c1 = c1n;
       r0 = r0n;
