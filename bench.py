@@ -71,6 +71,8 @@ def parse():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--parity-streams", type=int, default=64,
                     help="streams of the byte-parity sample when no CPU-baseline sample is run (N > 1)")
+    ap.add_argument("--no-other-configs", action="store_true",
+                    help="skip the short runs of the metric's other configurations (single-GPU default run only)")
     ap.add_argument("--probe", action="store_true",
                     help="instead of the benchmark: the latency probes (cycles of one dependent step, tans_probe)")
     ap.add_argument("--clocks-dir", default=None,
@@ -765,6 +767,42 @@ def check_parity(w, ref_stream, kind, dev):
             else "the oracle's C port"}
 
 
+OTHER_CONFIGS = ("laplace64", "gaussian_latent", "zipf_alias", "ragged_adaptive")
+
+
+def other_configs(args, dev):
+    """The metric's other configurations on this GPU, one short run each: device round trips timed
+    as the headline is (CUDA events, warm-up first, clocks sampled), a byte-parity sample against
+    the reference CPU (oracle/_ref) and the reference CPU's rate on that sample (not for the ragged
+    configuration, whose per-stream reference calls are timed by --workload ragged_adaptive)."""
+    import copy
+    out = {}
+    for name in OTHER_CONFIGS:
+        if name == args.workload:
+            continue
+        a = copy.copy(args)
+        a.workload, a.no_e2e, a.scale, a.length_scale = name, True, 1.0, 1.0
+        a.steps, a.warmup = max(1, min(args.steps, 5)), max(3, min(args.warmup, 3))
+        torch.cuda.empty_cache()
+        if name == "ragged_adaptive":
+            r = run_ours_ragged(a, 1, 0, dev.index or 0)
+            base = par = None
+        else:
+            r = run_ours(a, 1, 0, dev.index or 0)
+            base = par = None
+            if not args.no_cpu:
+                base, sample, ref_stream = cpu_reference(name, 2.0, 1.0, 1.0, steps=1, warmup=0, keep_sample=True)
+                par = check_parity(sample, ref_stream, base["kind"], dev)
+                del sample, ref_stream
+        out[name] = {"value": r["value"], "unit": UNIT, "ms_per_step": r["ms"], "steps": a.steps, "warmup": a.warmup,
+                     "push_ms": r["push_ms"], "pop_ms": r["pop_ms"], "streams": r["B"], "symbols": r["nsym"],
+                     "bit_exact_roundtrip": r["ok"], "gpu_launches": r["gpu_launches"], "clocks": r["clocks"],
+                     "roofline_frac": r["roofline"]["frac"], "roofline_kernel": r["roofline"]["kernel"],
+                     "cpu_baseline": base, "parity": par}
+        torch.cuda.empty_cache()
+    return out
+
+
 def reference_arm(args, ws, rank, cfg):
     """--impl reference: the reference's own CPU implementation only (rank 0)."""
     if rank == 0:
@@ -854,6 +892,10 @@ def main():
         for k in ("e2e", "weak_scaling"):
             if k in res:
                 line[k] = res[k]
+        if ws == 1 and args.workload == "mixture_invcdf" and args.scale == 1.0 and args.length_scale == 1.0 \
+                and not args.no_other_configs:
+            del res
+            line["other_configs"] = other_configs(args, dev)
         print(json.dumps(line), flush=True)
     if ws > 1:
         dist.barrier()
