@@ -39,6 +39,10 @@ def op_names(variant, interleave, alias_push, lookup):
 
 
 def same_rows(a, b):
+    """Equal shapes, lengths and records (state and words up to each row's length).  Columns that a
+    resize added past the old width are left uninitialised by the reference (rans.hpp:120-122:
+    `resize_` then the old rows copied back), so past the length only the rows' old width is
+    defined; test_push_onto_popped_stream_keeps_old_words compares that region too."""
     a, b = np.asarray(a), np.asarray(b)
     return a.shape == b.shape and np.array_equal(a[:, 0], b[:, 0]) and G.payload_bytes(a) == G.payload_bytes(b)
 
@@ -449,6 +453,38 @@ def test_push_steps_wider_than_the_precision(C, kernel, variant, monkeypatch):
                                   bypass_coding=False)
     assert C.device_status() == 0
     assert same_rows(st.cpu().numpy(), ref)
+
+
+@pytest.mark.parametrize("kernel", PUSH_KERNELS)
+@pytest.mark.parametrize("variant", VARIANTS)
+def test_push_onto_popped_stream_keeps_old_words(C, kernel, variant, monkeypatch):
+    """A stream pushed, popped back to its state and pushed again with fewer symbols needs no
+    resize for the second push: the reference writes only the words it emits and leaves every
+    other word of the row (the old words past the new length, and whatever the first resize left
+    in the new columns) as it was.  From the same whole tensor, the second push must leave exactly
+    the oracle's tensor (every push kernel, rows of 45 streams)."""
+    monkeypatch.setenv("TORCH_ANS_B200_PUSH_KERNEL", kernel)
+    B, N1, N2 = 45, 400, 120
+    rng = np.random.default_rng(zlib.crc32(f"repush-{kernel}-{variant}".encode()))
+    fp, push_c, sizes, offs, sym1, idx1 = _push_case(rng, variant, False, False, B, N1)
+    idx2 = rng.integers(0, push_c.shape[0], (B, N2)).astype(np.int32)
+    sym2 = (rng.integers(0, sizes[idx2] - 1) + offs[idx2]).astype(np.int32)
+    kw = dict(freq_precision=fp, bypass_coding=False, bypass_precision=4)
+    ref, e = O.push(variant, O.init_stream(variant, B), sym1, idx1, push_c, sizes, offs, fp, False)
+    assert e == 0
+    st = getattr(C, f"{variant}_init_stream")(B).cuda()
+    getattr(C, f"{variant}_push")(st, t(sym1), t(idx1), t(push_c), t(sizes), t(offs), **kw)
+    assert same_rows(st.cpu().numpy(), ref)
+    _, e = O.pop(variant, ref, idx1, push_c, sizes, offs, fp, False)
+    assert e == 0
+    getattr(C, f"{variant}_pop")(st, t(idx1), t(push_c), t(sizes), t(offs), **kw)
+    assert same_rows(st.cpu().numpy(), ref)
+    W = ref.shape[1]
+    ref2, e = O.push(variant, st.cpu().numpy(), sym2, idx2, push_c, sizes, offs, fp, False)
+    assert e == 0 and ref2.shape[1] == W  # no resize
+    getattr(C, f"{variant}_push")(st, t(sym2), t(idx2), t(push_c), t(sizes), t(offs), **kw)
+    assert C.device_status() == 0
+    assert st.shape[1] == W and np.array_equal(st.cpu().numpy(), ref2)
 
 
 @pytest.mark.parametrize("streams_per_block,chain_warps,prep_warps",

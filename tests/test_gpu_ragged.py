@@ -297,3 +297,56 @@ def _oracle_rows_push_only(variant, fp, lengths, sym, cdfs, sizes, offs):
         pushed.append(st)
         lo = hi
     return pushed, None, None
+
+
+@pytest.mark.parametrize("variant", VARIANTS)
+@pytest.mark.parametrize("kernel", ["lean", "warp"])
+def test_ragged_push_rows_too_short(variant, kernel, monkeypatch):
+    """Rows sized by the caller too short for their words (the C ABI): every push chain keeps the
+    words that fit, counts the rest in the length, flags TANS_DEV_OVERFLOW and never writes past
+    the row (guard words after the last row, and each row's neighbour, stay intact), exactly as the
+    oracle's per-stream pushes into rows of the same width do."""
+    from torch_ans_b200 import capi
+    _pick_pop(monkeypatch, kernel)
+    lib = capi.load()
+    rng = np.random.default_rng(zlib.crc32(f"ragged-ovf-{variant}".encode()))
+    lengths = [0, 2, 40, 300, 7, 120, 64]
+    fp, cdfs, sizes, offs, sym = _per_element_case(rng, variant, False, lengths)
+    B = len(lengths)
+    init = O.init_stream(variant, 1)
+    W = init.shape[1] + 5  # room for a few words only
+    host = np.zeros((B, W), np.int32)
+    host[:, : init.shape[1]] = init[0]
+    want, err_ref = [], 0
+    lo = 0
+    for n in lengths:
+        row = host[:1].copy()
+        if n:
+            e = O.lib().orc_push(O.VARIANTS[variant], 0, 1, O._ptr(row), 1, W, O._ptr(np.ascontiguousarray(sym[lo:lo + n])),
+                                 O._ptr(np.arange(n, dtype=np.int32)), n, O._ptr(np.ascontiguousarray(cdfs[lo:lo + n])),
+                                 n, cdfs.shape[1], O._ptr(np.ascontiguousarray(sizes[lo:lo + n])),
+                                 O._ptr(np.ascontiguousarray(offs[lo:lo + n])), fp, 0, 4, 1)
+            err_ref |= int(e)
+        want.append(row[0])
+        lo += n
+    assert err_ref & O.ERR_OVERFLOW
+    guard = 8
+    flat = torch.full((B * W + guard,), 0x5A5A5A5A, dtype=torch.int32, device="cuda")
+    flat[: B * W] = torch.from_numpy(host).cuda().reshape(-1)
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    s_d, c_d, z_d, o_d = dev(sym), dev(cdfs), dev(sizes), dev(offs)
+    rows = dev(np.concatenate([[0], np.cumsum(lengths)]).astype(np.int64))
+    T = len(sym)
+    ws = torch.empty(lib.tans_push_ragged_workspace_size(T) + 256, dtype=torch.uint8, device="cuda")
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    cs = torch.cuda.current_stream().cuda_stream
+    rc = lib.tans_push_ragged(capi.VARIANT[variant], flat.data_ptr(), B, W, s_d.data_ptr(), None, rows.data_ptr(), T,
+                              c_d.data_ptr(), T, cdfs.shape[1], z_d.data_ptr(), o_d.data_ptr(), fp, 0, 4,
+                              ws.data_ptr(), ws.numel(), status.data_ptr(), cs)
+    assert rc == 0
+    torch.cuda.synchronize()
+    assert int(status.item()) == err_ref
+    got = flat.cpu().numpy()
+    assert (got[B * W:] == 0x5A5A5A5A).all()
+    for b in range(B):
+        assert np.array_equal(got[b * W:(b + 1) * W], want[b]), f"stream {b} (length {lengths[b]})"

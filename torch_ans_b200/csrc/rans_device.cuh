@@ -16,8 +16,9 @@
 // 2^(N+l) + e with 0 <= e < d <= 2^l, so n*m / 2^(N+l) = n/d + n*e/(d*2^(N+l)) and the second
 // term is < 1/d; since n/d = floor(n/d) + j/d with j <= d-1 the floor is unchanged.  m fits in
 // W bits (m < 2^W for d >= 3, m = 2^N for d = 1 and 2), and floor(n*m / 2^(N+l)) =
-// mulhi_W(2n, m) >> l, so one form covers every divisor.  The push only divides a renormalised
-// state, which is < freq * 2^(state_bits-1-fp) <= 2^N, so the precondition n < 2^N holds.
+// mulhi_W(2n, m) >> l, so one form covers every divisor.  The fast push steps divide only a
+// renormalised state of a step with freq <= 2^fp, which is < freq * 2^(state_bits-1-fp) <= 2^N,
+// so the precondition n < 2^N holds there; the exact step code uses quotient_exact below.
 #pragma once
 
 #include <cstdint>
@@ -201,6 +202,24 @@ __device__ __forceinline__ void cp_async8(void* smem, const void* gmem) {
   const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
   asm volatile("cp.async.ca.shared.global [%0], [%1], 8;\n" ::"r"(s), "l"(gmem) : "memory");
 }
+// *p = v when c holds, as one predicated store (no branch around it); p addresses global memory
+template <typename W> __device__ __forceinline__ void st_global_if(W* p, uint32_t v, bool c);
+template <> __device__ __forceinline__ void st_global_if<uint8_t>(uint8_t* p, uint32_t v, bool c) {
+  asm volatile("{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %2, 0;\n\t@q st.global.u8 [%0], %1;\n}\n" ::"l"(p), "r"(v),
+               "r"((int)c)
+               : "memory");
+}
+template <> __device__ __forceinline__ void st_global_if<uint16_t>(uint16_t* p, uint32_t v, bool c) {
+  asm volatile("{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %2, 0;\n\t@q st.global.u16 [%0], %1;\n}\n" ::"l"(p), "r"(v),
+               "r"((int)c)
+               : "memory");
+}
+template <> __device__ __forceinline__ void st_global_if<uint32_t>(uint32_t* p, uint32_t v, bool c) {
+  asm volatile("{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %2, 0;\n\t@q st.global.u32 [%0], %1;\n}\n" ::"l"(p), "r"(v),
+               "r"((int)c)
+               : "memory");
+}
+
 __device__ __forceinline__ void cp_async4(void* smem, const void* gmem) {
   const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
   asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(s), "l"(gmem) : "memory");

@@ -189,14 +189,13 @@ __global__ void __launch_bounds__(512) push_ws_kernel(const PushParams P, int sb
             const uint32_t freq = e[q].z & 0xFFFFFFu;
             const unsigned long long bound = (unsigned long long)freq << shift;
             if constexpr (!ALIAS) {
-              // the word goes to the next slot unconditionally and the cursor advances only when
-              // it is kept: a slot past the row's length is undefined anyway, and the chunk check
-              // above keeps p + 1 inside the row, so the store needs no branch (measured faster
-              // here; slower on the alias step, whose remap load follows)
+              // the store is predicated on the word being kept (no branch; the chunk check above
+              // keeps p + 1 inside the row): slots past the row's length keep what they held, as
+              // the reference leaves them
 #pragma unroll
               for (int u = 0; u < MR; ++u) {
                 const bool r = (unsigned long long)x >= bound;
-                words[p + 1] = (W)x;
+                st_global_if<W>(words + (p + 1), (uint32_t)x, r);
                 p += r ? 1 : 0;
                 x = r ? (S)(x >> VT<V>::WB) : x;
               }

@@ -177,14 +177,14 @@ __global__ void __launch_bounds__(256) ragged_push_chain_kernel(const RaggedArgs
     r.rcap = 0;
     const uint32_t freq = packed ? entry_freq(r.e, true) : 0u;
     if (r.flags == 0u && freq - 1u < (1u << P.fp) && cur.p >= -1 && cur.p + MR < cur.cap) {
-      // every word this step can emit lands inside the row: the word goes to the next slot
-      // unconditionally and the cursor advances only when it is kept (a slot past the row's final
-      // length is never part of its record), so the renormalisation has no branch
+      // every word this step can emit lands inside the row: the store is predicated on the word
+      // being kept, so the renormalisation has no branch and slots past the row's final length
+      // keep what they held
       const S bound = (S)((S)freq << shift);
 #pragma unroll
       for (int u = 0; u < MR; ++u) {
         const bool rn = x >= bound;
-        words[cur.p + 1] = (W)x;
+        st_global_if<W>(words + (cur.p + 1), (uint32_t)x, rn);
         cur.p += rn ? 1 : 0;
         x = rn ? (S)(x >> VT<V>::WB) : x;
       }
@@ -207,7 +207,7 @@ __global__ void __launch_bounds__(256) ragged_push_chain_kernel(const RaggedArgs
 // (2 <= freq <= 2^fp) and whose words fit the row takes the fast form: the renormalisation count
 // from MR comparisons made at once ((x >> WB*t) >= bound for t < MR: the reference's loop of
 // rans_utils.hpp:45-49 runs exactly that many times, the conditions being nested), the words
-// stored unconditionally (the cursor advances only over the kept ones), the reciprocal quotient
+// stored by predicated stores (the kept ones only, no branch), the reciprocal quotient
 // mulhi(x, m) >> (l - 1) = floor(x * m / 2^(31+l)) (exact there: the renormalised state is below
 // bound <= 2^31) and C(s, x) of rans_utils.hpp:292.  Any other step runs push_chain, the
 // reference-exact step code, on the standard entry rebuilt from the second array.
@@ -284,13 +284,14 @@ __global__ void __launch_bounds__(256) ragged_push_lean_kernel(const RaggedArgs 
         int k;
         if constexpr (V == 1) {
           const uint32_t x8 = x >> 8, x16 = x >> 16;
-          k = (x >= bound ? 1 : 0) + (x8 >= bound ? 1 : 0) + (x16 >= bound ? 1 : 0);
-          wp[0] = (W)x;
-          wp[1] = (W)x8;
-          wp[2] = (W)x16;
+          const bool e0 = x >= bound, e1 = x8 >= bound, e2 = x16 >= bound;
+          k = (e0 ? 1 : 0) + (e1 ? 1 : 0) + (e2 ? 1 : 0);
+          st_global_if<W>(wp, x, e0);
+          st_global_if<W>(wp + 1, x8, e1);
+          st_global_if<W>(wp + 2, x16, e2);
         } else {
           k = x >= bound ? 1 : 0;
-          wp[0] = (W)x;
+          st_global_if<W>(wp, x, k != 0);
         }
         x >>= WB * k;
         p += k;
