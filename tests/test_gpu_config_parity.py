@@ -25,7 +25,8 @@ pytestmark = pytest.mark.gpu
 FIX = CC.load_fixture()
 RECT = [c.name for c in CC.CASES if c.builder != "ragged_adaptive"]
 PUSH_KERNELS = ["default", "ws", "chunk", "generic"]
-POP_VARIANTS = ["default", "lean_l1", "lean_bucket", "lean_bucket_plain_idx", "lean_split", "fast", "generic"]
+POP_VARIANTS = ["default", "lean_l1", "lean_l1_b10", "lean_bucket", "lean_bucket_plain_idx", "lean_split", "fast",
+                "generic"]
 
 
 @pytest.fixture(scope="module")
@@ -60,10 +61,12 @@ def expected(name):
 def _force(monkeypatch, push_kernel, pop_variant):
     if push_kernel != "default":
         monkeypatch.setenv("TORCH_ANS_B200_PUSH_KERNEL", push_kernel)
-    if pop_variant == "lean_l1":
+    if pop_variant in ("lean_l1", "lean_l1_b10"):
         monkeypatch.setenv("TORCH_ANS_B200_POP_KERNEL", "lean")
         monkeypatch.setenv("TORCH_ANS_B200_POP_LAYOUT", "bucket_global")
         monkeypatch.setenv("TORCH_ANS_B200_POP_L1", "1")
+        if pop_variant == "lean_l1_b10":  # level-1 entries of 1,024 cum values
+            monkeypatch.setenv("TORCH_ANS_B200_POP_L1_BITS", "10")
     elif pop_variant in ("lean_bucket", "lean_bucket_plain_idx"):
         monkeypatch.setenv("TORCH_ANS_B200_POP_KERNEL", "lean")
         monkeypatch.setenv("TORCH_ANS_B200_POP_LAYOUT", "bucket_global")

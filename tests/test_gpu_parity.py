@@ -611,8 +611,17 @@ def test_pop_heavy_tails_and_overrun(C, kernel, layout, lookup, variant, monkeyp
     assert same_rows(st.cpu().numpy(), ref_pop)
 
 
+def _set_l1(monkeypatch, l1):
+    """"0" / "1": level-1 table off / on at its default granularity; "1:b": on, 2^b cum values per
+    entry."""
+    on, _, bits = l1.partition(":")
+    monkeypatch.setenv("TORCH_ANS_B200_POP_L1", on)
+    if bits:
+        monkeypatch.setenv("TORCH_ANS_B200_POP_L1_BITS", bits)
+
+
 @pytest.mark.parametrize("iring", ["1", "0"])
-@pytest.mark.parametrize("l1", ["0", "1"])
+@pytest.mark.parametrize("l1", ["0", "1", "1:10", "1:12"])
 @pytest.mark.parametrize("lookup", ["search", "invcdf"])
 @pytest.mark.parametrize("variant", VARIANTS)
 def test_bucket_pop_zero_offsets_tails_and_bad_rows(C, lookup, variant, l1, iring, monkeypatch):
@@ -622,10 +631,11 @@ def test_bucket_pop_zero_offsets_tails_and_bad_rows(C, lookup, variant, l1, irin
     points past the row's end (a corrupted length the reference would read past the row for): the
     bucket pop must agree with the generic pop kernel, which takes the same exact step, and flag
     underflow.  With and without the level-1 table in shared memory, with the indexes through the
-    shared-memory ring fed by bulk copies and on plain loads."""
+    shared-memory ring fed by bulk copies and on plain loads; level-1 entries of 2^8 (the default
+    here), 2^10 and 2^12 cum values."""
     monkeypatch.setenv("TORCH_ANS_B200_POP_KERNEL", "lean")
     monkeypatch.setenv("TORCH_ANS_B200_POP_LAYOUT", "bucket_global")
-    monkeypatch.setenv("TORCH_ANS_B200_POP_L1", l1)
+    _set_l1(monkeypatch, l1)
     monkeypatch.setenv("TORCH_ANS_B200_POP_IRING", iring)
     rng = np.random.default_rng(zlib.crc32(f"bucket0-{lookup}-{variant}".encode()))
     fp = FP[variant]
@@ -706,7 +716,7 @@ def test_bucket_pop_short_rows_and_ring_boundaries(C, variant, iring, nchunks, m
     assert same_rows(st.cpu().numpy(), ref_pop)
 
 
-@pytest.mark.parametrize("l1", ["0", "1"])
+@pytest.mark.parametrize("l1", ["0", "1", "1:11"])
 @pytest.mark.parametrize("lookup", ["search", "invcdf"])
 @pytest.mark.parametrize("variant", VARIANTS)
 def test_bucket_pop_secondary_table_overflow(C, lookup, variant, l1, monkeypatch):
@@ -716,7 +726,7 @@ def test_bucket_pop_secondary_table_overflow(C, lookup, variant, l1, monkeypatch
     exact step.  Both must give the oracle's bytes, with and without the level-1 table."""
     monkeypatch.setenv("TORCH_ANS_B200_POP_KERNEL", "lean")
     monkeypatch.setenv("TORCH_ANS_B200_POP_LAYOUT", "bucket_global")
-    monkeypatch.setenv("TORCH_ANS_B200_POP_L1", l1)
+    _set_l1(monkeypatch, l1)
     rng = np.random.default_rng(zlib.crc32(f"secovf-{lookup}-{variant}".encode()))
     fp = FP[variant]
     A = 5000 if fp == 15 else 10000

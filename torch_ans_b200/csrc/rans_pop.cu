@@ -160,7 +160,7 @@ __global__ void build_bucket_kernel(const int32_t* cdfs, int64_t ntables, int64_
   }
 }
 
-// Level-1 table for few streams per SM: one entry per 2^l1b cum values (l1b = kL1Bits), in the
+// Level-1 table for few streams per SM: one entry per 2^l1b cum values (l1b >= kL1Bits), in the
 // bucket format, derived from the (exact) 16-cum entries: a coarse bucket is describable when its
 // fine entries all follow one two-symbol model -- a fine bucket before the boundary c1 repeats
 // (s0, c1, f0), the one holding c1 adds f1, one past it starts at c1 with symbol s0 + 1 and
@@ -458,8 +458,8 @@ static int64_t bucket_bytes(int64_t ntables, int fp) {
              : 0;
 }
 // level-1 table (ntables + 1 rows of 2^(fp - kL1Bits) entries), padded to 16 bytes
-static int64_t level1_bytes(int64_t ntables, int fp) {
-  return fp >= kL1Bits ? (((ntables + 1) * ((int64_t)8 << (fp - kL1Bits))) + 15) & ~(int64_t)15 : 0;
+static int64_t level1_bytes(int64_t ntables, int fp, int bits = kL1Bits) {
+  return fp >= bits ? (((ntables + 1) * ((int64_t)8 << (fp - bits))) + 15) & ~(int64_t)15 : 0;
 }
 
 static bool tables_enabled() {
@@ -698,14 +698,27 @@ int pop_impl(int variant, int lookup, int interleave, int32_t* stream, int64_t b
       smem = (size_t)ring + (size_t)popf_table_smem(tm, ntables, fp, cdf_width, sstride);
     }
   }
-  // level-1 table in shared memory in front of the bucket table: for at most two streams per SM
-  // (one lane per warp, so a level-1 miss costs only its own lane) when it fits beside the records
+  // level-1 table in shared memory in front of the bucket table, one entry per 2^l1_bits cum
+  // values (the finest granularity from 2^kL1Bits up that fits beside the records): chosen for at
+  // most two streams per SM (one lane per warp, so a level-1 miss costs only its own lane) with
+  // entries of at most 2^kL1AutoBits cum values.  Coarser entries are exact for fewer steps (the
+  // mixture tables at 2^10: 54 % of steps; the level-1 pop then measured slower than the bucket
+  // pop at 1,024 streams).  TORCH_ANS_B200_POP_L1=0|1 forces it off or on,
+  // TORCH_ANS_B200_POP_L1_BITS a granularity
   bool use_l1 = false;
+  int l1_bits = kL1Bits;
   if (tm == TM_BUCKET_GLOBAL && lean && fp >= kL1Bits) {
     const int env_l1 = env_int("TORCH_ANS_B200_POP_L1", -1);
-    const int64_t l1b = level1_bytes(ntables, fp);
-    use_l1 = (int64_t)smem + 16 + l1b <= kSmemBudget && (env_l1 == 1 || (env_l1 != 0 && batch <= 2 * (int64_t)dev_sms));
-    if (use_l1) smem += 16 + (size_t)l1b;
+    const int env_bits = env_int("TORCH_ANS_B200_POP_L1_BITS", 0);
+    if (env_bits >= kL1Bits && env_bits <= fp) {
+      l1_bits = env_bits;
+    } else {
+      while (l1_bits < fp && (int64_t)smem + 16 + level1_bytes(ntables, fp, l1_bits) > kSmemBudget) ++l1_bits;
+    }
+    const bool fits = (int64_t)smem + 16 + level1_bytes(ntables, fp, l1_bits) <= kSmemBudget;
+    const bool auto_on = batch <= 2 * (int64_t)dev_sms && l1_bits <= kL1AutoBits;
+    use_l1 = fits && (env_l1 == 1 || (env_l1 != 0 && auto_on));
+    if (use_l1) smem += 16 + (size_t)level1_bytes(ntables, fp, l1_bits);
   }
   // index ring of the bucket kernel (its bucket and fused-shared launches): per stream two halves
   // of kRingChunks index chunks and two mbarriers, after everything else in shared memory, when
@@ -731,7 +744,7 @@ int pop_impl(int variant, int lookup, int interleave, int32_t* stream, int64_t b
   if (need_fused) need += align_up((size_t)(ntables << fp) * 4) + align_up((size_t)(ntables << fp) * 2);
   if (need_split) need += align_up((size_t)(ntables << fp) * 2) + align_up((size_t)ntables * sstride * 4);
   if (need_bucket) need += align_up((size_t)bucket_bytes(ntables, fp));
-  if (use_l1) need += align_up((size_t)level1_bytes(ntables, fp));
+  if (use_l1) need += align_up((size_t)level1_bytes(ntables, fp, l1_bits));
   void* ws = workspace;
   bool owned = false;
   if (!ws && need > 0) {  // an empty table list needs no scratch at all
@@ -779,7 +792,8 @@ int pop_impl(int variant, int lookup, int interleave, int32_t* stream, int64_t b
       wsp += align_up((size_t)bucket_bytes(ntables, fp));
       if (use_l1) {
         P.fL1 = reinterpret_cast<unsigned long long*>(wsp);
-        P.l1_bytes = level1_bytes(ntables, fp);
+        P.l1_bytes = level1_bytes(ntables, fp, l1_bits);
+        P.l1_bits = l1_bits;
       }
     }
   }
@@ -815,9 +829,9 @@ int pop_impl(int variant, int lookup, int interleave, int32_t* stream, int64_t b
       else build_bucket_kernel<2, LK_SEARCH><<<bb, 128, 0, s>>>(cdfs, ntables, cdf_width, tinfo, fp, BK, SEC, sc, cnt);
     }
     if (use_l1) {
-      const int64_t n1 = (ntables + 1) << (fp - kL1Bits);
+      const int64_t n1 = (ntables + 1) << (fp - l1_bits);
       const int b1 = (int)std::max<int64_t>(1, std::min<int64_t>((n1 + 127) / 128, 16 * (int64_t)dev_sms));
-      build_level1_kernel<<<b1, 128, 0, s>>>(BK, ntables, fp, kL1Bits, const_cast<unsigned long long*>(P.fL1));
+      build_level1_kernel<<<b1, 128, 0, s>>>(BK, ntables, fp, l1_bits, const_cast<unsigned long long*>(P.fL1));
       note_launch();
     }
   }

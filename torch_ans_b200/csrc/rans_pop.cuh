@@ -32,6 +32,7 @@ struct PopParams {
   int64_t sec_cap;                // blocks the secondary table holds
   const unsigned long long* fL1;  // bucket layout: level-1 table staged in shared memory (or null)
   int64_t l1_bytes;               // its bytes (a multiple of 16; 0: no level-1 table)
+  int l1_bits;                    // log2 of the cum values one level-1 entry covers
   int spt;             // streams per thread (fast kernel)
   int fused_smem;      // fused table staged in shared memory
   int tin_smem;        // per-table info staged in shared memory

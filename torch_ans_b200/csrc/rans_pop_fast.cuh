@@ -25,6 +25,7 @@ namespace tans {
 enum : int { TM_FUSED_SMEM = 0, TM_FUSED_GLOBAL = 1, TM_SPLIT_SMEM = 2, TM_SPLIT_GLOBAL = 3, TM_BUCKET_GLOBAL = 4 };
 constexpr int kBucketBits = 4;  // bucket layout: 16 cum values per bucket
 constexpr int kL1Bits = 8;      // level-1 table in shared memory: 256 cum values per entry
+constexpr int kL1AutoBits = 8;  // coarsest level-1 entry (cum values, log2) chosen without being asked
 constexpr int POPF_RS = 8;  // index ring slots (chunks of 4)
 constexpr int POPF_L = 6;   // chunks between an index load and its use
 

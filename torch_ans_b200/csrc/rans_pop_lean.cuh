@@ -346,7 +346,7 @@ __global__ void __maxnreg__(96) pop_bucket_kernel(const __grid_constant__ PopPar
   // row (the shared region holds 32 bytes per table, these use 24 + 8)
   TableInfo* tsm = reinterpret_cast<TableInfo*>(smem_raw);
   int2* tsm2 = reinterpret_cast<int2*>(tsm + P.ntables);
-  // level-1 table (L1): one entry per 2^kL1Bits cum values, copied in by the whole block; or
+  // level-1 table (L1): one entry per 2^P.l1_bits cum values, copied in by the whole block; or
   // (FUSED) the fused D and S tables of every table, staged by bulk copies
   unsigned char* l1s = popf_align16(smem_raw + P.ntables * 32);
   const int64_t m = P.ntables << P.fp;
@@ -408,8 +408,9 @@ __global__ void __maxnreg__(96) pop_bucket_kernel(const __grid_constant__ PopPar
   // entry addresses: the bucket table's row of table k, or with L1 the level-1 row in shared
   // memory (a 32-bit shared address), plus the entry's byte offset taken from the state's low word
   const uint32_t l1base = smem_u32(l1s);
-  const uint32_t l1rowbytes = 8u << (P.fp - kL1Bits);
-  const uint32_t l1mask = (cmask >> kL1Bits) << 3;
+  const uint32_t l1rowbytes = 8u << (P.fp - P.l1_bits);
+  const uint32_t l1mask = (cmask >> P.l1_bits) << 3;
+  const uint32_t l1shift = (uint32_t)P.l1_bits - 3u;
   // FUSED: entry index (k << fp) | cum into the shared D and S tables; a table index outside the
   // list reads table 0 and is flagged separately (the fused tables have no marker row)
   const uint32_t fdbase = smem_u32(tD), fsbase = smem_u32(tS);
@@ -420,7 +421,7 @@ __global__ void __maxnreg__(96) pop_bucket_kernel(const __grid_constant__ PopPar
     else return bk0 + (uintptr_t)min((uint32_t)k, kmark) * rowbytes;
   };
   auto addr_of = [&](uintptr_t rowp, uint32_t lowword) -> uintptr_t {
-    if constexpr (L1) return rowp + ((lowword >> (kL1Bits - 3)) & l1mask);
+    if constexpr (L1) return rowp + ((lowword >> l1shift) & l1mask);
     else if constexpr (FUSED) return rowp + (lowword & cmask);
     else return rowp | ((lowword >> 1) & bmask);
   };
