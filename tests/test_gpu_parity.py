@@ -510,6 +510,48 @@ def test_ws_push_block_shapes(C, streams_per_block, chain_warps, prep_warps, var
     assert same_rows(st.cpu().numpy(), ref)
 
 
+@pytest.mark.parametrize("alias", [False, True])
+@pytest.mark.parametrize("variant", VARIANTS)
+def test_ws_push_many_blocks(C, variant, alias, monkeypatch):
+    """The warp-specialised push at the launch shape of a large batch (8,192 streams: ~56 streams
+    per block on every SM, more prep tasks than prep threads), with escapes: every row must match
+    the oracle's.  Raw symbols and indexes pass through each block's shared-memory ring, so this
+    checks the hand-over at the block shape the large workloads use."""
+    monkeypatch.setenv("TORCH_ANS_B200_PUSH_KERNEL", "ws")
+    B, N = 8192, 96
+    rng = np.random.default_rng(zlib.crc32(f"wsmany-{variant}-{alias}".encode()))
+    fp, push_c, sizes, offs, sym, idx = _push_case(rng, variant, alias, True, B, N)
+    ref, perr = O.push(variant, O.init_stream(variant, B), sym, idx, push_c, sizes, offs, fp, True, 4, alias=alias)
+    assert perr == 0
+    st = getattr(C, f"{variant}_init_stream")(B).cuda()
+    op = f"{variant}_alias_push" if alias else f"{variant}_push"
+    getattr(C, op)(st, t(sym), t(idx), t(push_c), t(sizes), t(offs), freq_precision=fp, bypass_coding=True,
+                   bypass_precision=4)
+    assert C.device_status() == 0
+    assert same_rows(st.cpu().numpy(), ref)
+
+
+@pytest.mark.parametrize("ntables", [256, 257, 3000])
+@pytest.mark.parametrize("variant", VARIANTS)
+def test_ws_push_table_counts(C, variant, ntables, monkeypatch):
+    """The warp-specialised push keeps 16 interleaved copies of the per-table {size, offset}
+    records for up to 256 tables and one copy beyond: both sides of that limit, with escapes and
+    table offsets, must give the oracle's rows."""
+    monkeypatch.setenv("TORCH_ANS_B200_PUSH_KERNEL", "ws")
+    B, N = 300, 128
+    rng = np.random.default_rng(zlib.crc32(f"wstables-{variant}-{ntables}".encode()))
+    fp, cdfs, sizes, offs = _random_case(rng, variant, True, K=ntables, A=20)
+    idx = rng.integers(0, ntables, (B, N)).astype(np.int32)
+    sym = (rng.integers(-4, 26, (B, N)) + offs[idx]).astype(np.int32)
+    ref, perr = O.push(variant, O.init_stream(variant, B), sym, idx, cdfs, sizes, offs, fp, True, 4)
+    assert perr == 0
+    st = getattr(C, f"{variant}_init_stream")(B).cuda()
+    getattr(C, f"{variant}_push")(st, t(sym), t(idx), t(cdfs), t(sizes), t(offs), freq_precision=fp,
+                                  bypass_coding=True, bypass_precision=4)
+    assert C.device_status() == 0
+    assert same_rows(st.cpu().numpy(), ref)
+
+
 @pytest.mark.parametrize("kernel", PUSH_KERNELS)
 @pytest.mark.parametrize("variant", VARIANTS)
 def test_push_row_overflow_matches_oracle(kernel, variant, monkeypatch):

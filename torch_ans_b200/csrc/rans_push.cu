@@ -402,8 +402,10 @@ int push_impl(int variant, int use_alias, int interleave, int32_t* stream, int64
     const int64_t M = (int64_t)1 << fp;
     const int64_t remap = use_alias ? ntables * M : 0;
     const int64_t budget = 200 * 1024;
-    const bool rsmem = use_alias && pushws_smem_bytes(1, true, ntables, remap) <= budget;
-    const int64_t fixed = pushws_smem_bytes(0, use_alias != 0, ntables, rsmem ? remap : 0);
+    const int tc_env = env_int("TORCH_ANS_B200_PUSHWS_TCOPIES", 0);
+    const int tcopies = (tc_env == 1 || tc_env == 16) ? tc_env : pushws_tcopies(ntables);
+    const bool rsmem = use_alias && pushws_smem_bytes(1, true, ntables, remap, tcopies) <= budget;
+    const int64_t fixed = pushws_smem_bytes(0, use_alias != 0, ntables, rsmem ? remap : 0, tcopies);
     const int64_t per = pushws_stream_bytes(use_alias != 0);
     const int64_t sb_max = fixed < budget ? (budget - fixed) / per : 0;
     int64_t sb = (batch + dev_sms - 1) / dev_sms;
@@ -422,6 +424,7 @@ int push_impl(int variant, int use_alias, int interleave, int32_t* stream, int64
       const int blocks = (int)((batch + sb - 1) / sb);
       const size_t smem = (size_t)(fixed + sb * per);
       P.lanes = (int)lanes;
+      P.ws_tcopies = tcopies;
       const int wl = env_int("TORCH_ANS_B200_WAIT_LIMIT", -1);
       P.wait_limit = wl >= 0 ? (unsigned)wl : WS_WAIT_LIMIT;
       bool ok;

@@ -28,6 +28,7 @@ struct PushParams {
   int vec;
   int tin_smem;  // per-table info staged in shared memory
   unsigned wait_limit;  // tries of each bounded hand-over wait (warp-specialised kernel)
+  int ws_tcopies;       // warp-specialised kernel: copies of the per-table {size, offset} records (1 or 16)
 };
 
 // ---------------------------------------------------------------- step pieces

@@ -48,9 +48,13 @@ inline int64_t pushws_stream_bytes(bool alias) {
          + (int64_t)WS_R * 4                        // flag words
          + (alias ? (int64_t)WS_R * 4 * WS_G * 4 : 0);  // alias: table index per symbol
 }
-inline int64_t pushws_smem_bytes(int64_t sb, bool alias, int64_t ntables, int64_t remap_entries) {
-  return WS_HEADER + sb * pushws_stream_bytes(alias) + ntables * 16 + remap_entries * 4;
+inline int64_t pushws_smem_bytes(int64_t sb, bool alias, int64_t ntables, int64_t remap_entries, int tcopies) {
+  return WS_HEADER + sb * pushws_stream_bytes(alias) + ntables * (16 + 8 * (int64_t)tcopies) + remap_entries * 4;
 }
+// Copies of the per-table {size, offset} records the prep warps gather at random table indexes:
+// with 16 interleaved copies, lane l reads copy l % 16, so the 16 lanes of a half warp always read
+// 16 different 8-byte bank pairs (no bank conflicts); one copy when 16 would take over 32 KB.
+inline int pushws_tcopies(int64_t ntables) { return ntables * 8 * 16 <= 32 * 1024 ? 16 : 1; }
 
 // chain state the rare exact path reads and writes, passed by value both ways so that the kernel
 // never takes the address of its state or of its parameters (both stay in registers)
@@ -97,10 +101,12 @@ __global__ void __launch_bounds__(512) push_ws_kernel(const PushParams P, int sb
   unsigned long long* empty = full + WS_R;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + WS_R);
   uint4* ent = reinterpret_cast<uint4*>(smem_raw + WS_HEADER);                 // [R][4G][sb]
-  int4* rsym = reinterpret_cast<int4*>(ent + (size_t)WS_R * 4 * WS_G * sb);    // [RR][sb][G]
-  int4* ridx = rsym + (size_t)WS_RR * sb * WS_G;                               // [RR][sb][G]
+  int4* rsym = reinterpret_cast<int4*>(ent + (size_t)WS_R * 4 * WS_G * sb);    // [RR][G][sb]
+  int4* ridx = rsym + (size_t)WS_RR * sb * WS_G;                               // [RR][G][sb]
   TableInfo* tsm = reinterpret_cast<TableInfo*>(ridx + (size_t)WS_RR * sb * WS_G);
-  uint32_t* flg = reinterpret_cast<uint32_t*>(tsm + P.ntables);                // [R][sb]
+  int2* tso = reinterpret_cast<int2*>(tsm + P.ntables);                          // [K][copies] {size, offset}
+  const int tcl = P.ws_tcopies == 16 ? 4 : 0;                                    // log2 of the copies
+  uint32_t* flg = reinterpret_cast<uint32_t*>(tso + (P.ntables << tcl));        // [R][sb]
   int32_t* kix = reinterpret_cast<int32_t*>(flg + (size_t)WS_R * sb);          // [R][4G][sb]
   int32_t* rsm = kix + (ALIAS ? (size_t)WS_R * 4 * WS_G * sb : 0);
 
@@ -113,6 +119,10 @@ __global__ void __launch_bounds__(512) push_ws_kernel(const PushParams P, int sb
   const int ngr = (nch + WS_G - 1) / WS_G;
 
   for (int64_t k = tid; k < P.ntables; k += T) tsm[k] = P.tinfo[k];
+  for (int64_t i = tid; i < (P.ntables << tcl); i += T) {
+    const TableInfo ti = P.tinfo[i >> tcl];
+    tso[i] = make_int2(ti.size, ti.offset);
+  }
   if constexpr (ALIAS && RSMEM) {
     for (int64_t i = tid; i < P.ntables * M; i += T) {
       const int64_t k = i >> P.fp, r = i & (M - 1);
@@ -252,19 +262,30 @@ __global__ void __launch_bounds__(512) push_ws_kernel(const PushParams P, int sb
 
   // -------------------------------------------------------------------- prep warps
   const int ptid = tid - chain_warps * 32;
-  const int ntask = WS_G * sb;
   const uint32_t kmax = (uint32_t)(P.ntables - 1);
   const int64_t emax = P.enc_stride - 1;
+  // Tasks run stream-fastest across the lanes (task t: chunk t / sbp of stream t % sbp), in the
+  // copies of the raw symbols and indexes and in the prep alike: every thread reads back only the
+  // raw chunks its own cp.async copies brought in (its cp.async wait covers them), and a warp's
+  // raw-ring reads, entry-ring copies and flag bytes fall on consecutive slots (no bank conflicts).
+  // From 32 streams per block up, sbp = sb rounded up to whole warps, so that every warp works on
+  // one chunk of consecutive streams; below that sbp = sb (padding would leave most lanes idle:
+  // the prep warps' instructions, not bank conflicts, then set their pace).
+  const int sbp = sb >= 32 ? (sb + 31) & ~31 : sb;
+  const int ntaskp = WS_G * sbp;
+  // t / sbp as a multiply-shift: exact for t * sbp < 2^20 (t < 4 sbp, sbp <= 128 streams)
+  const uint32_t sbm = ((1u << 20) + (uint32_t)sbp - 1u) / (uint32_t)sbp;
+  const int tcm = (1 << tcl) - 1;
   auto issue_raw = [&](int gr) {
     const int rs = gr % WS_RR;
-    for (int t = ptid; t < ntask; t += nprep) {
-      const int c = t % WS_G, s = t / WS_G;
+    for (int t = ptid; t < ntaskp; t += nprep) {
+      const int c = (int)(((uint32_t)t * sbm) >> 20), s = t - c * sbp;
       const int64_t b = b0 + s;
       const int gc = gr * WS_G + c;
-      if (b < P.batch && gc < nch) {
+      if (s < sb && b < P.batch && gc < nch) {
         const int64_t off = b * N + 4 * (int64_t)(nch - 1 - gc);
-        cp_async16(rsym + ((size_t)rs * sb + s) * WS_G + c, P.sym + off, 16);
-        cp_async16(ridx + ((size_t)rs * sb + s) * WS_G + c, P.idx + off, 16);
+        cp_async16(rsym + ((size_t)rs * WS_G + c) * sb + s, P.sym + off, 16);
+        cp_async16(ridx + ((size_t)rs * WS_G + c) * sb + s, P.idx + off, 16);
       }
     }
     cp_async_commit();  // one group per call, empty or not, so the wait depths below hold
@@ -284,23 +305,23 @@ __global__ void __launch_bounds__(512) push_ws_kernel(const PushParams P, int sb
     }
     const int rs = g % WS_RR;
     uint8_t* fb = reinterpret_cast<uint8_t*>(flg + (size_t)slot * sb);
-    for (int t = ptid; t < ntask; t += nprep) {
-      const int c = t % WS_G, s = t / WS_G;
+    for (int t = ptid; t < ntaskp; t += nprep) {  // the same task order as issue_raw
+      const int c = (int)(((uint32_t)t * sbm) >> 20), s = t - c * sbp;
       const int64_t b = b0 + s;
       const int gc = g * WS_G + c;
-      if (b >= P.batch || gc >= nch) continue;
-      const int4 s4 = rsym[((size_t)rs * sb + s) * WS_G + c];
-      const int4 k4 = ridx[((size_t)rs * sb + s) * WS_G + c];
+      if (s >= sb || b >= P.batch || gc >= nch) continue;
+      const int4 s4 = rsym[((size_t)rs * WS_G + c) * sb + s];
+      const int4 k4 = ridx[((size_t)rs * WS_G + c) * sb + s];
       const int32_t sv[4] = {s4.x, s4.y, s4.z, s4.w}, kv[4] = {k4.x, k4.y, k4.z, k4.w};
       bool exact = false;
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         const uint32_t kc = min((uint32_t)kv[q], kmax);
         exact |= (uint32_t)kv[q] > kmax;
-        const TableInfo ti = tsm[kc];
-        const int32_t v = (int32_t)((uint32_t)sv[q] - (uint32_t)ti.offset);
-        exact |= v < 0 || v >= ti.size - 1 || (int64_t)v > emax;
-        if constexpr (BYPASS) exact |= v >= ti.size - 2;  // escape slot or beyond: escape coding
+        const int2 ti = tso[((int)kc << tcl) + (lane & tcm)];  // {size, offset}, this lane's copy
+        const int32_t v = (int32_t)((uint32_t)sv[q] - (uint32_t)ti.y);
+        exact |= v < 0 || v >= ti.x - 1 || (int64_t)v > emax;
+        if constexpr (BYPASS) exact |= v >= ti.x - 2;  // escape slot or beyond: escape coding
         const int64_t vc = min((int64_t)max(v, 0), emax);
         const size_t eo = ((size_t)slot * 4 * WS_G + 4 * c + q) * sb + s;
         cp_async16(ent + eo, P.enc + (int64_t)kc * P.enc_stride + vc, 16);
