@@ -722,10 +722,14 @@ int pop_impl(int variant, int lookup, int interleave, int32_t* stream, int64_t b
   }
   // index ring of the bucket kernel (its bucket and fused-shared launches): per stream two halves
   // of kRingChunks index chunks and two mbarriers, after everything else in shared memory, when
-  // it fits (TORCH_ANS_B200_POP_IRING=0 keeps the indexes on plain loads)
+  // it fits; not with the level-1 table for rans32 (byte words), where it measured slower
+  // (gaussian_latent pop 9.06 vs 7.09 ms; laplace64, rans64 with the level-1 table: 5.53 with
+  // the ring vs 6.29 ms without).  TORCH_ANS_B200_POP_IRING=0|1 forces plain loads or the ring.
   int64_t iring_off = 0;
   bool iring = false;
-  if (lean && (tm == TM_BUCKET_GLOBAL || tm == TM_FUSED_SMEM) && env_int("TORCH_ANS_B200_POP_IRING", 1) != 0) {
+  const int env_ir = env_int("TORCH_ANS_B200_POP_IRING", -1);
+  const bool want_ring = env_ir == 1 || (env_ir != 0 && !(use_l1 && variant == TANS_RANS32));
+  if (lean && (tm == TM_BUCKET_GLOBAL || tm == TM_FUSED_SMEM) && want_ring) {
     const int64_t nsl = (int64_t)(L.threads / 32) * L.lanes;
     const int64_t off = ((int64_t)smem + 15) & ~(int64_t)15;
     if (off + nsl * kRingBytesPerStream <= kSmemBudget) {
