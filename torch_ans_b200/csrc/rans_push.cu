@@ -413,7 +413,9 @@ int push_impl(int variant, int use_alias, int interleave, int32_t* stream, int64
     if (sb_env > 0) sb = sb_env;
     sb = std::min<int64_t>(sb, std::min<int64_t>(sb_max, 128));
     if (sb >= 1) {
-      int64_t cw = std::min<int64_t>(env_int("TORCH_ANS_B200_PUSHWS_CHAIN_WARPS", 4), sb);
+      // chain warps: up to 4, with at least 4 lanes each (zipf_alias, 7 streams per block: 2 warps
+      // of 4 lanes took 32.7 vs 34.4 ms for 4 warps of 2 at a quarter length)
+      int64_t cw = std::min<int64_t>(env_int("TORCH_ANS_B200_PUSHWS_CHAIN_WARPS", (int)std::min<int64_t>(4, (sb + 3) / 4)), sb);
       cw = std::max<int64_t>(1, std::min<int64_t>(cw, 8));
       // whole lanes per chain warp, then only the warps those lanes need
       const int64_t lanes = std::min<int64_t>(32, (sb + cw - 1) / cw);
