@@ -413,9 +413,10 @@ int push_impl(int variant, int use_alias, int interleave, int32_t* stream, int64
     if (sb_env > 0) sb = sb_env;
     sb = std::min<int64_t>(sb, std::min<int64_t>(sb_max, 128));
     if (sb >= 1) {
-      // chain warps: up to 4, with at least 4 lanes each (zipf_alias, 7 streams per block: 2 warps
-      // of 4 lanes took 32.7 vs 34.4 ms for 4 warps of 2 at a quarter length)
-      int64_t cw = std::min<int64_t>(env_int("TORCH_ANS_B200_PUSHWS_CHAIN_WARPS", (int)std::min<int64_t>(4, (sb + 3) / 4)), sb);
+      // chain warps: up to 4, with about 7 lanes or more each (mixture tables at a quarter length:
+      // 7 streams per block 4.88 ms on 1 warp vs 4.97 on 2; 14 streams 5.01 on 2 warps vs 5.28 on
+      // 4; 28 streams 5.30 on 4 vs 5.31 on 2; 56 streams: 4 warps best)
+      int64_t cw = std::min<int64_t>(env_int("TORCH_ANS_B200_PUSHWS_CHAIN_WARPS", (int)std::min<int64_t>(4, (sb + 6) / 7)), sb);
       cw = std::max<int64_t>(1, std::min<int64_t>(cw, 8));
       // whole lanes per chain warp, then only the warps those lanes need
       const int64_t lanes = std::min<int64_t>(32, (sb + cw - 1) / cw);
